@@ -1,0 +1,410 @@
+"""Benchmark: decode tok/s of a Qwen2.5-3B-shape W8A16 model, batch 64.
+
+Workload (the configuration the headline metric is quoted
+on): one mixed scheduler step of a random-init Qwen2.5-3B-shaped decoder
+(36 layers, hidden 2048, 16/2 heads, head_dim 128, intermediate 11008, vocab
+151936, tied bf16 lm_head, int8 per-channel layer weights, bf16 KV, block
+size 16): 64 decode sequences at context 2048 plus one 512-token prefill
+chunk. A "step" is one pass of the whole hot path over that batch; the
+decode throughput is 64 tokens per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl pageserve_b200|reference]
+
+value: decode tok/s over K CUDA-graph replays of the step, inputs resident in
+HBM (the step streams ~8 GB of weights + KV, far larger than the 126 MB L2,
+so no flush is needed between steps).
+e2e: the same metric through the public step API (StepGraph.run): per step a
+host->device copy of token ids + metadata from pinned memory and a
+device->host read of the 65 greedy next tokens.
+--gpus N > 1: N independent replicas, one per GPU (weak scaling); tensor
+parallelism is not wired into this benchmark yet.
+--impl reference: the reference algorithm's CPU path (the oracle port of
+engine/model.py, one forward_step per sequence as engine/runner.py:65-79
+does), on a bounded sample of the same workload, all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s (Qwen2.5-3B-shape W8A16, bs64)"
+UNIT = "tok/s"
+N_DECODE, CTX, PREFILL = 64, 2048, 512
+BLOCK = 16
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def _config(extra=None):
+    c = {"workload": "BASELINE config 4: Qwen2.5-3B-shape int8 mixed step, 64 decode seqs @ctx 2048 "
+                     "+ one 512-token prefill chunk, block 16",
+         "model": "qwen2.5-3b-shape (random init)", "layers": 36, "global_batch": N_DECODE,
+         "prefill_tokens_per_step": PREFILL, "seq_len": CTX, "kv_dtype": "bf16", "weights": "int8 per-channel",
+         "l2": "inputs larger than L2 (~8 GB streamed per step)"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+# --------------------------------------------------------------- clocks ----
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workload ----
+
+def build_workload(device, seed=0):
+    import numpy as np
+    import torch
+
+    from pageserve_b200 import synthetic
+    from pageserve_b200.model import PagedCausalLM
+
+    shape = synthetic.QWEN25_3B
+    sd = synthetic.TorchStateDict(shape, seed=seed, device=device)
+    m = PagedCausalLM.from_state_dict(sd, shape, device=device, dtype=torch.bfloat16, quantize=True,
+                                      max_position=4096)
+    del sd
+    torch.cuda.empty_cache()
+    nblk_dec = CTX // BLOCK
+    nblk_pre = PREFILL // BLOCK
+    num_blocks = N_DECODE * nblk_dec + nblk_pre + 64
+    m.allocate_kv_cache(num_blocks, BLOCK)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 7)
+    for c in (m.k_cache, m.v_cache):
+        c.normal_(0.0, 1.0, generator=g)
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(num_blocks)
+    tables, at = [], 0
+    for _ in range(N_DECODE):
+        tables.append(perm[at:at + nblk_dec].tolist())
+        at += nblk_dec
+    tables.append(perm[at:at + nblk_pre].tolist())
+    q_lens = [1] * N_DECODE + [PREFILL]
+    start_pos = [CTX - 1] * N_DECODE + [0]
+    ids = rng.integers(0, shape.vocab, size=N_DECODE + PREFILL).astype(np.int64)
+    return m, dict(q_lens=q_lens, start_pos=start_pos, tables=tables, ids=ids, shape=shape)
+
+
+def time_events(fn, iters, stream=None):
+    import torch
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(iters):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters  # ms
+
+
+def kernel_breakdown(m, w, peaks):
+    """Each main kernel of the step timed alone with CUDA events, rotating
+    over the 36 layers' weights / caches so nothing is served from L2."""
+    import torch
+
+    from pageserve_b200.paged_attention import AttentionWorkspace, paged_attention
+    from pageserve_b200.quantization import LinearWorkspace, linear16, w8a16_linear
+
+    dev = m.device
+    T = N_DECODE + PREFILL
+    L = len(m.fused)
+    H, I = m.hidden_size, m.intermediate_size
+    x_h = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
+    x_i = torch.randn(T, I, device=dev, dtype=torch.bfloat16)
+    x_a = torch.randn(T, m.num_heads * m.head_dim, device=dev, dtype=torch.bfloat16)
+    ws = LinearWorkspace()
+    res = {}
+
+    def lin(name, x, get_w):
+        outs = {}
+        ctr = [0]
+
+        def f():
+            wgt = get_w(m.fused[ctr[0] % L])
+            ctr[0] += 1
+            outs["y"] = w8a16_linear(x, wgt.q, wgt.scale, workspace=ws)
+        f()
+        ms = time_events(f, 2 * L)
+        wgt = get_w(m.fused[0])
+        N, K = wgt.q.shape
+        M = x.shape[0]
+        flops = 2.0 * M * N * K
+        byts = N * K + 4 * N + 2 * M * K + 2 * M * N
+        res[name] = {"ms": ms, "M": M, "N": N, "K": K, "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6,
+                     "flops": flops, "bytes": byts}
+
+    lin("qkv", x_h, lambda f: f.qkv)
+    lin("o_proj", x_a, lambda f: f.o)
+    lin("gate_up", x_h, lambda f: f.gate_up)
+    lin("down", x_i, lambda f: f.down)
+    # lm_head on the 65 sampled rows
+    xl = torch.randn(N_DECODE + 1, H, device=dev, dtype=torch.bfloat16)
+    f = lambda: linear16(xl, m.lm_head_w, workspace=ws)  # noqa: E731
+    f()
+    ms = time_events(f, 5)
+    V = m.lm_head_w.shape[0]
+    byts = V * H * 2 + 2 * xl.shape[0] * (H + V)
+    res["lm_head"] = {"ms": ms, "M": xl.shape[0], "N": V, "K": H, "gbs": byts / ms / 1e6, "bytes": byts,
+                      "tflops": 2.0 * xl.shape[0] * V * H / ms / 1e9, "flops": 2.0 * xl.shape[0] * V * H}
+    # decode attention: 64 sequences at ctx 2048, rotating over layer caches
+    meta = m.make_meta([1] * N_DECODE, [CTX - 1] * N_DECODE, w["tables"][:N_DECODE])
+    q = torch.randn(N_DECODE, m.num_heads, m.head_dim, device=dev, dtype=torch.bfloat16)
+    aws = AttentionWorkspace()
+    ctr = [0]
+
+    def att():
+        li = ctr[0] % L
+        ctr[0] += 1
+        paged_attention(q, m.k_cache[li], m.v_cache[li], meta.block_tables, meta.cu_q, meta.start_pos, 1, CTX,
+                        workspace=aws)
+    att()
+    ms = time_events(att, 2 * L)
+    kv = N_DECODE * CTX * m.num_kv_heads * m.head_dim * 2 * 2
+    byts = kv + 2 * 2 * N_DECODE * m.num_heads * m.head_dim + 4 * N_DECODE * (CTX // BLOCK)
+    res["attn_decode"] = {"ms": ms, "gbs": byts / ms / 1e6, "bytes": byts}
+    return res
+
+
+def cpu_baseline_sample(layers_sampled=1, decode_seqs_sampled=4):
+    """The reference algorithm on the host cores (oracle port of
+    engine/model.py, per-sequence forward_step like engine/runner.py:65-79):
+    a 1-layer 3B-shape model runs `decode_seqs_sampled` decode sequences at
+    context 2048 and the 512-token prefill chunk; per-layer and head time are
+    scaled to 36 layers and 64 decode sequences."""
+    import numpy as np
+    import torch
+
+    from oracle.model import OracleCausalLM
+    from pageserve_b200 import synthetic
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    shape = synthetic.QWEN25_3B.with_layers(layers_sampled)
+    sd = synthetic.generate_state_dict(shape, seed=0)
+    o = OracleCausalLM(sd, shape, quantize=True, max_position=4096)
+    del sd
+    nb = (decode_seqs_sampled + 1) * (CTX // BLOCK) + 40
+    o.allocate_kv_cache(nb, BLOCK)
+    rng = np.random.default_rng(1)
+    o.k_cache[:] = rng.standard_normal(o.k_cache.shape, dtype=np.float32)
+    o.v_cache[:] = o.k_cache
+    tabs = [list(range(i * (CTX // BLOCK), (i + 1) * (CTX // BLOCK))) for i in range(decode_seqs_sampled + 1)]
+    t_dec, t_pre = {}, {}
+    t0 = time.perf_counter()
+    for i in range(decode_seqs_sampled):
+        o.forward_step([int(rng.integers(0, shape.vocab))], tabs[i], CTX - 1, timings=t_dec)
+    o.forward_step(rng.integers(0, shape.vocab, size=PREFILL), tabs[-1], 0, timings=t_pre)
+    wall = time.perf_counter() - t0
+    per_dec = (t_dec["layers"] / layers_sampled * 36 + t_dec["head"]) / decode_seqs_sampled
+    step = N_DECODE * per_dec + (t_pre["layers"] / layers_sampled * 36 + t_pre["head"])
+    return {"value": N_DECODE / step, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"oracle port of the reference step (numpy/BLAS, per-sequence forward_step); "
+                       f"{layers_sampled} of 36 layers, {decode_seqs_sampled} of 64 decode seqs + the 512-token "
+                       f"chunk, scaled to the full step; sample wall {wall:.1f} s"),
+            "step_s": step}
+
+
+# ------------------------------------------------------------------ run ----
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    cb = None
+    for i in range(max(1, args.warmup) + max(1, args.steps)):
+        cb = cpu_baseline_sample()
+        if i >= max(1, args.warmup):
+            vals.append(cb["value"])
+    v = statistics.median(vals)
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * N_DECODE / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random init)",
+            "config": _config({"parallelism": "host CPU"}), "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cb["cores"], "kind": "port", "sample": cb["sample"]},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    from pageserve_b200 import _lib
+    from pageserve_b200.model import StepGraph
+
+    peaks = _peaks()
+    m, w = build_workload(device, seed=rank)
+    max_blocks = max(len(t) for t in w["tables"])
+    g = StepGraph(m, w["q_lens"], max_blocks, CTX, w["start_pos"], w["tables"], w["ids"])
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    with Clocks(local) as clk:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        dist.barrier()
+    launches = g.launches_per_replay * args.steps + (_lib.launch_count() - launches0)
+    # e2e: host inputs -> public step API -> host next tokens
+    for _ in range(2):
+        g.run(w["ids"], w["start_pos"], w["tables"])
+    torch.cuda.synchronize()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        g.run(w["ids"], w["start_pos"], w["tables"])
+    e_end.record()
+    torch.cuda.synchronize()
+    e_ms = e_start.elapsed_time(e_end)
+    _lib.raise_on_device_error()
+    if world > 1:
+        t = torch.tensor([ms, e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e_ms = t.tolist()
+    value = world * N_DECODE * args.steps / (ms / 1e3)
+    e2e = world * N_DECODE * args.steps / (e_ms / 1e3)
+    kb = kernel_breakdown(m, w, peaks) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        dist.destroy_process_group() if world > 1 else None
+        return
+    # dominant kernel: the largest per-step time share among the measured classes
+    per_step = {k: v["ms"] * (36 if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode") else 1)
+                for k, v in kb.items()}
+    dom = max(per_step, key=per_step.get)
+    d = kb[dom]
+    tensor_bound = dom in ("qkv", "o_proj", "gate_up", "down") and d["flops"] / peaks["bf16_tflops"] / 1e12 > \
+        d["bytes"] / peaks["hbm_gbs"] / 1e9
+    if tensor_bound:
+        roof = {"kernel": dom, "bound": "tensor", "achieved": d["tflops"], "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": d["tflops"] / peaks["bf16_tflops"], "traffic": None,
+                "algorithmic_per_launch": d["flops"], "peak_source": peaks["source"] + " (burst)"}
+    else:
+        roof = {"kernel": dom, "bound": "hbm", "achieved": d["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": d["gbs"] / peaks["hbm_gbs"], "traffic": None, "algorithmic_per_launch": d["bytes"],
+                "peak_source": peaks["source"]}
+    cpu = cpu_baseline_sample() if not args.no_cpu_baseline else None
+    clocks = clk.summary()
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random init, random KV contents)",
+            "config": _config({"parallelism": f"replicas x{world}" if world > 1 else "single GPU"}),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": g.h2d_bytes, "d2h_bytes_per_step": g.d2h_bytes,
+                    "api": "StepGraph.run (host ids/metadata in, host next tokens out)"},
+            "gpu_launches": launches, "launches_per_step": g.launches_per_replay,
+            "roofline": roof,
+            "kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
+                        for k, v in kb.items()},
+            "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="pageserve_b200", choices=["pageserve_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

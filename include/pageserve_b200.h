@@ -1,0 +1,182 @@
+/*
+ * pageserve_b200 — C ABI of the B200-native (sm_100a) decode-step hot path.
+ *
+ * Plain pointers and sizes only. Every pointer argument named *_dev is a CUDA
+ * device pointer on the current device; `stream` is a cudaStream_t (pass the
+ * caller's current stream, e.g. torch.cuda.current_stream().cuda_stream).
+ * Calls are asynchronous with respect to the host unless stated otherwise.
+ *
+ * Return value: PS_OK (0) or a PS_ERR_* code; ps_last_error() then returns a
+ * human-readable message (thread-local). Host-side validation runs before any
+ * launch, so an error return means nothing was launched. Kernels never trap:
+ * device-side range violations (a block id outside the pool, a token id
+ * outside the vocabulary) skip the access and are recorded in a per-device
+ * status word read by ps_device_status().
+ *
+ * Layouts (row-major, innermost last):
+ *   KV cache       [num_blocks][block_size][num_kv_heads][head_dim]   (one layer)
+ *   block tables   int32 [num_seqs][max_blocks_per_seq]
+ *   q / attention  [tokens][num_q_heads][head_dim]
+ *   int8 weight    int8 [N][K] with float32 scale [N]  (per output channel)
+ *   activations    [M][K]
+ *
+ * The reference these entry points replace is Rakshit-gen/pageserve; each
+ * declaration cites the reference function (file:line) whose behaviour it
+ * reproduces.
+ */
+#ifndef PAGESERVE_B200_H_
+#define PAGESERVE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define PS_API __attribute__((visibility("default")))
+#else
+#define PS_API
+#endif
+
+typedef struct CUstream_st* ps_stream_t; /* == cudaStream_t */
+
+enum ps_dtype { PS_F32 = 0, PS_BF16 = 1, PS_F16 = 2, PS_I8 = 3 };
+
+enum ps_status {
+  PS_OK = 0,
+  PS_ERR_INVALID = 1,     /* bad shape / dtype / null pointer  (Python: ValueError/TypeError) */
+  PS_ERR_INDEX = 2,       /* block table too short, position out of range (Python: IndexError) */
+  PS_ERR_CUDA = 3,        /* a CUDA runtime call failed (Python: RuntimeError) */
+  PS_ERR_UNSUPPORTED = 4, /* shape/dtype this build has no kernel for (Python: NotImplementedError) */
+  PS_ERR_DEVICE = 5,      /* the device status word holds an error (Python: RuntimeError) */
+  PS_ERR_TIMEOUT = 6      /* a bounded device wait gave up (Python: TimeoutError) */
+};
+
+/* ---------------------------------------------------------------- library */
+
+/* ABI version of this header (bumped on any signature change). */
+PS_API int ps_abi_version(void);
+/* Message of the last error returned on this host thread. */
+PS_API const char* ps_last_error(void);
+/* Number of kernels this library has launched in this process. */
+PS_API uint64_t ps_launch_count(void);
+/* Reads (and with clear != 0, clears) the current device's status word after
+ * synchronising `stream`. *code receives 0 or a device error code
+ * (1 block id, 2 slot, 3 token id, 4 wait timeout, 5 metadata). */
+PS_API int ps_device_status(int* code, int clear, ps_stream_t stream);
+
+/* ------------------------------------------------------- (a1) KV writes */
+
+/* engine/paged_attention.py:62-79 (write_kv): copy k[i], v[i] (rows of
+ * num_kv_heads*head_dim elements) to slot block_table[(start_pos+i)/bs]*bs +
+ * (start_pos+i)%bs of k_cache / v_cache. Bit-exact (a copy). table_len is the
+ * number of entries of block_table_dev; start_pos+num_tokens must fit in
+ * table_len*block_size (else PS_ERR_INDEX, like the reference's list index). */
+PS_API int ps_write_kv(void* k_cache_dev, void* v_cache_dev, const int32_t* block_table_dev, int table_len,
+                int num_blocks, int block_size, int num_kv_heads, int head_dim, int dtype, int start_pos,
+                int num_tokens, const void* k_dev, const void* v_dev, ps_stream_t stream);
+
+/* Batched form of the slot mapping used by write_kv (engine/paged_attention.py:74-77)
+ * for a step of several sequences: for sequence b with chunk tokens
+ * [cu_q[b], cu_q[b+1]) starting at position start_pos[b], writes
+ * positions[t] = start_pos[b] + (t - cu_q[b]) and
+ * slots[t] = block_tables[b][pos / bs] * bs + pos % bs  (int32). */
+PS_API int ps_build_slot_mapping(int32_t* positions_dev, int32_t* slots_dev, const int32_t* block_tables_dev,
+                          int max_blocks_per_seq, const int32_t* cu_q_dev, const int32_t* start_pos_dev,
+                          int num_seqs, int total_tokens, int num_blocks, int block_size, ps_stream_t stream);
+
+/* ------------------------------------------- (a2-a5) paged attention */
+
+/* Scratch bytes ps_paged_attention needs for these launch bounds (0 when
+ * no split of the context is used). */
+PS_API size_t ps_paged_attention_workspace_size(int num_seqs, int max_q_len, int max_ctx, int num_q_heads,
+                                         int num_kv_heads, int head_dim);
+
+/* engine/paged_attention.py:117-132 (paged_causal_attention_incremental),
+ * batched over sequences, with gather_kv (:82-99) fused away: the kernel reads
+ * the cache blocks in place through the block table. Sequence b's queries are
+ * rows [cu_q[b], cu_q[b+1]) of q, at absolute positions start_pos[b] + i; its
+ * context is start_pos[b] + (cu_q[b+1]-cu_q[b]) tokens; query row i attends to
+ * key positions <= start_pos[b] + i (causal_attention_incremental, :16-50),
+ * q head h reads kv head h / (num_q_heads/num_kv_heads), scale
+ * 1/sqrt(head_dim). max_q_len / max_ctx are host upper bounds over the batch
+ * (they size the grid; the kernel reads the true values on the device).
+ * dtype PS_BF16 or PS_F16; head_dim 64 or 128. */
+PS_API int ps_paged_attention(void* out_dev, const void* q_dev, const void* k_cache_dev, const void* v_cache_dev,
+                       const int32_t* block_tables_dev, int max_blocks_per_seq, const int32_t* cu_q_dev,
+                       const int32_t* start_pos_dev, int num_seqs, int total_q, int max_q_len, int max_ctx,
+                       int num_blocks, int block_size, int num_q_heads, int num_kv_heads, int head_dim,
+                       int dtype, void* workspace_dev, size_t workspace_bytes, ps_stream_t stream);
+
+/* ------------------------------------------------ (a6-a7) W8A16 linear */
+
+/* engine/quantization.py:16-23 (quantize_per_channel) on the device:
+ * scale[n] = max(max_k |w[n,k]|, 1e-8) / 127 (float32),
+ * q[n,k] = clamp(round_half_even(w[n,k] / scale[n]), -127, 127). w is float32
+ * or bf16 (dtype). Bit-exact against the reference for float32 input. */
+PS_API int ps_quantize_per_channel(int8_t* q_dev, float* scale_dev, const void* w_dev, int dtype, int N, int K,
+                            ps_stream_t stream);
+
+/* engine/quantization.py:26-50 + F.linear (engine/model.py:168-190):
+ * y[m,n] = scale[n] * sum_k x[m,k] * q[n,k] + bias[n] + residual[m,n]
+ * (bias, residual optional: pass NULL). x, y, residual, bias in `dtype`
+ * (PS_BF16/PS_F16 use the tensor-core path for M > 16; PS_F32 runs on CUDA
+ * cores). Accumulates in float32. Equivalent to the reference's
+ * dequantize-then-matmul with the dequantized weight kept in float32. */
+PS_API size_t ps_w8a16_linear_workspace_size(int M, int N, int K);
+PS_API int ps_w8a16_linear(void* y_dev, const void* x_dev, const int8_t* q_dev, const float* scale_dev,
+                    const void* bias_dev, const void* residual_dev, int M, int N, int K, int dtype,
+                    void* workspace_dev, size_t workspace_bytes, ps_stream_t stream);
+
+/* Plain linear with a 16-bit weight (the unquantized lm_head,
+ * engine/model.py:193): y[m,n] = sum_k x[m,k] * w[n,k] (+ bias). */
+PS_API int ps_linear(void* y_dev, const void* x_dev, const void* w_dev, const void* bias_dev, const void* residual_dev,
+              int M, int N, int K, int dtype, void* workspace_dev, size_t workspace_bytes, ps_stream_t stream);
+
+/* Fused SwiGLU MLP input: out[m,i] = silu(gu[m,i]) * gu[m, I+i] where gu is
+ * [gate | up] (engine/model.py:188-190). */
+PS_API int ps_silu_mul(void* out_dev, const void* gate_up_dev, int M, int I, int dtype, ps_stream_t stream);
+
+/* -------------------------------------------------- (a8-a9) norm / rope */
+
+/* engine/model.py:29-34 (rms_norm) fused with the residual add of
+ * engine/model.py:184,190: when residual_dev != NULL,
+ * r = x + residual (rounded to dtype, stored to residual_out_dev when that is
+ * non-NULL), else r = x; y = r * rsqrt(mean(r^2) + eps) * weight, float32
+ * math, one rounding to dtype. */
+PS_API int ps_rmsnorm(void* y_dev, void* residual_out_dev, const void* x_dev, const void* residual_dev,
+               const void* weight_dev, float eps, int M, int H, int dtype, ps_stream_t stream);
+
+/* engine/model.py:50-54 (apply_rope) with explicit per-token cos/sin rows
+ * (T, D) in `dtype`: out = x*cos + rotate_half(x)*sin, x (T, H, D). */
+PS_API int ps_apply_rope(void* out_dev, const void* x_dev, const void* cos_dev, const void* sin_dev, int T, int H,
+                  int D, int dtype, ps_stream_t stream);
+
+/* engine/model.py:168-178 fused: from the fused projection output
+ * qkv[t] = [q (Hq*D) | k (Hkv*D) | v (Hkv*D)] (bias already added), rotate q
+ * and k by position positions[t] (NeoX half rotation, cos/sin from the float32
+ * table rope_cos/rope_sin [max_pos][D/2]) and write q to q_out (T, Hq, D), the
+ * rotated k and v to slot slots[t] of the paged caches (write_kv,
+ * engine/paged_attention.py:62-79). slots[t] < 0 skips the cache write. */
+PS_API int ps_rope_qkv_write_kv(void* q_out_dev, void* k_cache_dev, void* v_cache_dev, const void* qkv_dev,
+                         const int32_t* positions_dev, const int32_t* slots_dev, const float* rope_cos_dev,
+                         const float* rope_sin_dev, int max_pos, int T, int num_q_heads, int num_kv_heads,
+                         int head_dim, int num_slots, int dtype, ps_stream_t stream);
+
+/* ------------------------------------------------------- (a10) the step */
+
+/* F.embedding (engine/model.py:159): out[t] = table[ids[t]]. */
+PS_API int ps_embedding(void* out_dev, const int64_t* ids_dev, const void* table_dev, int T, int H, int vocab,
+                 int dtype, ps_stream_t stream);
+
+/* Greedy next token, int(logits[row].argmax()) (server.py:51): first index of
+ * the maximum of each row; logits (M, V) in dtype; out int32 [M]. */
+PS_API int ps_argmax(int32_t* out_dev, const void* logits_dev, int M, int V, int ld, int dtype, ps_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGESERVE_B200_H_ */

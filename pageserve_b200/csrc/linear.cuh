@@ -1,0 +1,15 @@
+// Internal dispatch between the linear kernels.
+#pragma once
+#include "common.cuh"
+
+namespace ps_host {
+// CUDA-core weight-streaming kernel (any M; chosen for small M).
+int linear_simt(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
+                const void* resid, int M, int N, int K, int dtype, cudaStream_t s);
+// tcgen05 tensor-core kernel (bf16/f16 activations). Returns PS_ERR_UNSUPPORTED
+// when the shape has no tensor-core configuration.
+int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
+              const void* resid, int M, int N, int K, int dtype, void* workspace, size_t workspace_bytes,
+              cudaStream_t s);
+size_t linear_tc_workspace(int M, int N, int K);
+}  // namespace ps_host

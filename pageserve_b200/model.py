@@ -1,0 +1,441 @@
+"""Drop-in for the reference's engine/model.py on the sm_100a kernels.
+
+``PagedCausalLM`` keeps the reference's constructor, ``allocate_kv_cache``,
+``forward_step`` and attributes (``device``, ``dtype``, ``config``,
+``layers``, ``k_cache``, ``v_cache``, ``block_size``, ...), and adds
+``forward_batch`` — one pass over a whole scheduler step (many decode
+sequences plus chunked-prefill chunks) from device-resident block tables —
+and ``capture_decode_graph`` for CUDA-graph replay of a decode step.
+
+Per layer the step runs (engine/model.py:164-190):
+  rmsnorm -> fused QKV W8A16 linear (+bias) -> RoPE + KV-slot write ->
+  paged attention -> o_proj W8A16 (+residual) -> rmsnorm ->
+  fused gate|up W8A16 -> SiLU*up -> down_proj W8A16 (+residual)
+then the final rmsnorm, the bf16 lm_head and an on-device argmax.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+from . import _lib
+from .batch import attention_runs, pack_metadata
+from .paged_attention import AttentionWorkspace, paged_attention
+from .quantization import LinearWorkspace, QuantizedWeight, linear16, w8a16_linear
+
+Weight = torch.Tensor | QuantizedWeight
+
+
+# ------------------------------------------------------- reference ops ----
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """engine/model.py:29-34 as one fused kernel (float32 math)."""
+    return rms_norm_fused(x, weight, eps)
+
+
+def rms_norm_fused(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+                   residual_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = rmsnorm(x [+ residual]) * weight; the sum is also stored to
+    residual_out when given (engine/model.py:29-34, 184, 190). Replaces the
+    reference's Triton kernel (kernels/rmsnorm_triton.py:46-57)."""
+    _lib.require_cuda(x, weight, residual)
+    H = x.shape[-1]
+    x2 = x.reshape(-1, H).contiguous()
+    if out is None:
+        out = torch.empty_like(x2)
+    w = weight.to(x.dtype).contiguous()
+    r = None if residual is None else residual.reshape(-1, H).contiguous()
+    _lib.check(_lib.load().ps_rmsnorm(out.data_ptr(), _lib.ptr(residual_out), x2.data_ptr(), _lib.ptr(r),
+                                      w.data_ptr(), float(eps), x2.shape[0], H, _lib.dtype_code(x.dtype),
+                                      _lib.stream_ptr(x.device)), "rmsnorm")
+    return out.reshape(x.shape)
+
+
+# The reference's Triton entry point name (kernels/rmsnorm_triton.py:46).
+rms_norm_triton = rms_norm
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    """engine/model.py:37-39."""
+    x1, x2 = x.chunk(2, dim=-1)
+    return torch.cat((-x2, x1), dim=-1)
+
+
+def build_rope_cache(max_len: int, head_dim: int, theta: float, device, dtype):
+    """engine/model.py:42-47 (init-time table)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device).float() / head_dim))
+    t = torch.arange(max_len, device=device).float()
+    freqs = torch.outer(t, inv_freq)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def build_rope_table_f32(max_len: int, head_dim: int, theta: float, device):
+    """float32 (max_len, head_dim/2) cos/sin halves for the fused RoPE kernel
+    (same formula as engine/model.py:42-47, kept in float32)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device).float() / head_dim))
+    t = torch.arange(max_len, device=device).float()
+    freqs = torch.outer(t, inv_freq)
+    return freqs.cos().contiguous(), freqs.sin().contiguous()
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """engine/model.py:50-54: x (T, H, D), cos/sin (T, D)."""
+    _lib.require_cuda(x, cos, sin)
+    T, H, D = x.shape
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    c = cos.to(x.dtype).contiguous()
+    s = sin.to(x.dtype).contiguous()
+    _lib.check(_lib.load().ps_apply_rope(out.data_ptr(), x.data_ptr(), c.data_ptr(), s.data_ptr(), T, H, D,
+                                         _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)), "apply_rope")
+    return out
+
+
+@dataclass
+class LayerWeights:
+    """engine/model.py:57-70."""
+    input_ln: torch.Tensor
+    post_ln: torch.Tensor
+    q_w: Weight
+    k_w: Weight
+    v_w: Weight
+    o_w: Weight
+    gate_w: Weight
+    up_w: Weight
+    down_w: Weight
+    q_b: torch.Tensor | None = None
+    k_b: torch.Tensor | None = None
+    v_b: torch.Tensor | None = None
+
+
+@dataclass
+class FusedLayer:
+    """Kernel-side layout of one layer: projections sharing an input are
+    concatenated along N (per-channel scales make this exact)."""
+    input_ln: torch.Tensor
+    post_ln: torch.Tensor
+    qkv: Weight
+    qkv_b: torch.Tensor
+    o: Weight
+    gate_up: Weight
+    down: Weight
+
+
+def _cat_weights(ws: list[Weight], dtype) -> Weight:
+    if isinstance(ws[0], QuantizedWeight):
+        return QuantizedWeight.from_quantized(torch.cat([w.q for w in ws], 0), torch.cat([w.scale for w in ws], 0),
+                                              dtype)
+    return torch.cat(ws, 0).contiguous()
+
+
+class StepMeta:
+    """Device-resident metadata of one step (int32)."""
+
+    def __init__(self, block_tables: torch.Tensor, cu_q: torch.Tensor, start_pos: torch.Tensor, q_lens: list[int],
+                 ctx_lens: list[int]):
+        self.block_tables = block_tables
+        self.cu_q = cu_q
+        self.start_pos = start_pos
+        self.q_lens = q_lens
+        self.ctx_lens = ctx_lens
+
+
+class PagedCausalLM:
+    """engine/model.py:73-193 on the sm_100a kernels."""
+
+    def __init__(self, model_id: str, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                 quantize: bool = False):
+        from transformers import AutoConfig, AutoModelForCausalLM
+
+        config = AutoConfig.from_pretrained(model_id)
+        hf = AutoModelForCausalLM.from_pretrained(model_id, torch_dtype=torch.float32)
+        sd = hf.state_dict()
+        del hf
+        rope_params = getattr(config, "rope_parameters", None)
+        theta = rope_params["rope_theta"] if rope_params else config.rope_theta
+        self._init(config, sd, device, dtype, quantize, theta)
+
+    @classmethod
+    def from_state_dict(cls, state_dict: dict, shape, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                        quantize: bool = True, max_position: int | None = None) -> "PagedCausalLM":
+        """Build from an HF-named state dict (numpy or torch tensors) and a
+        ``synthetic.Qwen2Shape`` (the seeded random-init checkpoints)."""
+        cfg = SimpleNamespace(num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
+                              hidden_size=shape.hidden, head_dim=shape.head_dim, rms_norm_eps=shape.rms_eps,
+                              rope_theta=shape.rope_theta, rope_parameters=None,
+                              max_position_embeddings=max_position or shape.max_position,
+                              num_hidden_layers=shape.num_layers, vocab_size=shape.vocab,
+                              intermediate_size=shape.intermediate, tie_word_embeddings=shape.tie_embeddings)
+        obj = cls.__new__(cls)
+        obj._init(cfg, state_dict, device, dtype, quantize, shape.rope_theta)
+        return obj
+
+    def _init(self, config, sd, device, dtype, quantize, theta):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback)")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        _lib.load()
+        _lib.ensure_status_word(self.device)
+        self.dtype = dtype
+        self.quantize = quantize
+        self.config = config
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.hidden_size = config.hidden_size
+        self.head_dim = getattr(config, "head_dim", None) or self.hidden_size // self.num_heads
+        self.rms_eps = config.rms_norm_eps
+        self.rope_theta = theta
+        self.max_position_embeddings = config.max_position_embeddings
+
+        def T(key):
+            v = sd[key]
+            return (torch.from_numpy(np.ascontiguousarray(v)) if isinstance(v, np.ndarray) else v)
+
+        def dev(key, dt=None):
+            return T(key).to(device=self.device, dtype=dt or dtype).contiguous()
+
+        def load_weight(key) -> Weight:
+            w = T(key).to(self.device)
+            if quantize:
+                qw = QuantizedWeight(w)
+                qw.dtype = dtype
+                return qw
+            return w.to(dtype).contiguous()
+
+        self.embed_tokens = dev("model.embed_tokens.weight")
+        self.final_norm_w = dev("model.norm.weight")
+        self.lm_head_w = dev("lm_head.weight") if "lm_head.weight" in sd else self.embed_tokens
+        self.layers: list[LayerWeights] = []
+        self.fused: list[FusedLayer] = []
+        for i in range(config.num_hidden_layers):
+            p = f"model.layers.{i}."
+            lw = LayerWeights(
+                input_ln=dev(p + "input_layernorm.weight"),
+                post_ln=dev(p + "post_attention_layernorm.weight"),
+                q_w=load_weight(p + "self_attn.q_proj.weight"),
+                k_w=load_weight(p + "self_attn.k_proj.weight"),
+                v_w=load_weight(p + "self_attn.v_proj.weight"),
+                o_w=load_weight(p + "self_attn.o_proj.weight"),
+                gate_w=load_weight(p + "mlp.gate_proj.weight"),
+                up_w=load_weight(p + "mlp.up_proj.weight"),
+                down_w=load_weight(p + "mlp.down_proj.weight"),
+                q_b=dev(p + "self_attn.q_proj.bias") if p + "self_attn.q_proj.bias" in sd else None,
+                k_b=dev(p + "self_attn.k_proj.bias") if p + "self_attn.k_proj.bias" in sd else None,
+                v_b=dev(p + "self_attn.v_proj.bias") if p + "self_attn.v_proj.bias" in sd else None,
+            )
+            self.layers.append(lw)
+            hq, hkv, d = self.num_heads, self.num_kv_heads, self.head_dim
+            zb = lambda n: torch.zeros(n, dtype=dtype, device=self.device)  # noqa: E731
+            qkv_b = torch.cat([lw.q_b if lw.q_b is not None else zb(hq * d),
+                               lw.k_b if lw.k_b is not None else zb(hkv * d),
+                               lw.v_b if lw.v_b is not None else zb(hkv * d)]).contiguous()
+            self.fused.append(FusedLayer(
+                input_ln=lw.input_ln, post_ln=lw.post_ln,
+                qkv=_cat_weights([lw.q_w, lw.k_w, lw.v_w], dtype), qkv_b=qkv_b, o=lw.o_w,
+                gate_up=_cat_weights([lw.gate_w, lw.up_w], dtype), down=lw.down_w))
+        self.intermediate_size = (self.layers[0].gate_w.shape[0] if self.layers else 0)
+        self.vocab_size = self.embed_tokens.shape[0]
+        self.cos_cache, self.sin_cache = build_rope_cache(self.max_position_embeddings, self.head_dim, theta,
+                                                          self.device, dtype)
+        self.rope_cos, self.rope_sin = build_rope_table_f32(self.max_position_embeddings, self.head_dim, theta,
+                                                            self.device)
+        self.attn_ws = AttentionWorkspace()
+        self.lin_ws = LinearWorkspace()
+        self.k_cache = None
+        self.v_cache = None
+        self.block_size = None
+
+    # ------------------------------------------------------------ memory --
+    def allocate_kv_cache(self, num_blocks: int, block_size: int) -> None:
+        """engine/model.py:143-147: (L, NB, bs, Hkv, D) zeros."""
+        shape = (len(self.layers), num_blocks, block_size, self.num_kv_heads, self.head_dim)
+        self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+
+    # ------------------------------------------------------------- linear --
+    def _linear(self, x, w: Weight, bias=None, residual=None):
+        if isinstance(w, QuantizedWeight):
+            return w8a16_linear(x, w.q, w.scale, bias, residual, workspace=self.lin_ws)
+        return linear16(x, w, bias, residual, workspace=self.lin_ws)
+
+    # -------------------------------------------------------------- steps --
+    def make_meta(self, q_lens: list[int], start_pos: list[int], block_tables: list[list[int]],
+                  max_blocks: int | None = None) -> StepMeta:
+        """Host lists -> device int32 metadata (one host->device copy).
+        Raises IndexError when a block table is too short for its context
+        (engine/paged_attention.py:77) or names a block outside the pool."""
+        buf, B, mb, ctx = pack_metadata(q_lens, start_pos, block_tables, self.block_size, self.num_blocks,
+                                        max_blocks)
+        d = torch.from_numpy(buf).to(self.device, non_blocking=False)
+        return StepMeta(d[2 * B + 1:].view(B, mb), d[:B + 1], d[B + 1:2 * B + 1], list(q_lens), ctx)
+
+    def _forward(self, ids: torch.Tensor, meta: StepMeta, logits_rows: torch.Tensor | None):
+        T = ids.shape[0]
+        H, hq, hkv, d = self.hidden_size, self.num_heads, self.num_kv_heads, self.head_dim
+        lib = _lib.load()
+        stream = _lib.stream_ptr(self.device)
+        x = torch.empty((T, H), dtype=self.dtype, device=self.device)
+        _lib.check(lib.ps_embedding(x.data_ptr(), ids.data_ptr(), self.embed_tokens.data_ptr(), T, H,
+                                    self.vocab_size, _lib.dtype_code(self.dtype), stream), "embedding")
+        positions = torch.empty(T, dtype=torch.int32, device=self.device)
+        slots = torch.empty(T, dtype=torch.int32, device=self.device)
+        B = len(meta.q_lens)
+        _lib.check(lib.ps_build_slot_mapping(positions.data_ptr(), slots.data_ptr(), meta.block_tables.data_ptr(),
+                                             meta.block_tables.shape[1], meta.cu_q.data_ptr(),
+                                             meta.start_pos.data_ptr(), B, T, self.num_blocks, self.block_size,
+                                             stream), "build_slot_mapping")
+        runs = attention_runs(meta.q_lens, hq // hkv)
+        q = torch.empty((T, hq, d), dtype=self.dtype, device=self.device)
+        attn = torch.empty((T, hq, d), dtype=self.dtype, device=self.device)
+        num_slots = self.num_blocks * self.block_size
+        for li, fl in enumerate(self.fused):
+            h = rms_norm_fused(x, fl.input_ln, self.rms_eps)
+            qkv = self._linear(h, fl.qkv, fl.qkv_b)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            _lib.check(lib.ps_rope_qkv_write_kv(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), qkv.data_ptr(),
+                                                positions.data_ptr(), slots.data_ptr(), self.rope_cos.data_ptr(),
+                                                self.rope_sin.data_ptr(), self.max_position_embeddings, T, hq, hkv,
+                                                d, num_slots, _lib.dtype_code(self.dtype), stream), "rope_qkv")
+            for (s, e, _) in runs:
+                paged_attention(q, kc, vc, meta.block_tables[s:e], meta.cu_q[s:e + 1], meta.start_pos[s:e],
+                                max(meta.q_lens[s:e]), max(meta.ctx_lens[s:e]), out=attn, workspace=self.attn_ws)
+            x = self._linear(attn.view(T, hq * d), fl.o, residual=x)
+            h = rms_norm_fused(x, fl.post_ln, self.rms_eps)
+            gu = self._linear(h, fl.gate_up)
+            act = torch.empty((T, self.intermediate_size), dtype=self.dtype, device=self.device)
+            _lib.check(lib.ps_silu_mul(act.data_ptr(), gu.data_ptr(), T, self.intermediate_size,
+                                       _lib.dtype_code(self.dtype), stream), "silu_mul")
+            x = self._linear(act, fl.down, residual=x)
+        if logits_rows is not None:
+            x = x.index_select(0, logits_rows)
+        x = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
+        return linear16(x, self.lm_head_w, workspace=self.lin_ws)
+
+    def forward_step(self, input_ids: torch.Tensor, block_table: list[int], start_pos: int) -> torch.Tensor:
+        """engine/model.py:149-193: one chunk of one sequence; returns
+        (chunk_len, vocab) logits."""
+        if self.k_cache is None:
+            raise RuntimeError("allocate_kv_cache() must run before forward_step()")
+        ids = input_ids.to(device=self.device, dtype=torch.int64).reshape(-1)
+        T = ids.shape[0]
+        meta = self.make_meta([T], [int(start_pos)], [list(block_table)])
+        return self._forward(ids, meta, None)
+
+    def forward_batch(self, input_ids, q_lens: list[int], start_pos: list[int], block_tables: list[list[int]],
+                      return_logits: bool = True):
+        """One scheduler step for many sequences in one pass (superset of the
+        reference, which calls forward_step once per sequence,
+        engine/runner.py:65-79). input_ids: the chunks concatenated in
+        sequence order. Returns (logits of each sequence's last token (B, V),
+        greedy next tokens int32 (B,))."""
+        if self.k_cache is None:
+            raise RuntimeError("allocate_kv_cache() must run before forward_batch()")
+        ids = torch.as_tensor(input_ids, dtype=torch.int64).to(self.device).reshape(-1)
+        meta = self.make_meta(q_lens, start_pos, block_tables)
+        last = meta.cu_q[1:].to(torch.int64) - 1
+        logits = self._forward(ids, meta, last)
+        nxt = self.argmax(logits)
+        return (logits if return_logits else None), nxt
+
+    def argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        """int(logits[row].argmax()) for every row, on the device."""
+        M, V = logits.shape
+        out = torch.empty(M, dtype=torch.int32, device=logits.device)
+        _lib.check(_lib.load().ps_argmax(out.data_ptr(), logits.data_ptr(), M, V, logits.stride(0),
+                                         _lib.dtype_code(logits.dtype), _lib.stream_ptr(logits.device)), "argmax")
+        return out
+
+
+class StepGraph:
+    """CUDA-graph replay of one ``forward_batch`` shape (the graph-capturable
+    decode the reference's engine/cuda_graphs.py:17-26 asks for: block tables
+    and start positions live in device buffers refreshed by copies, so one
+    captured graph serves every step of the same batch shape).
+
+    Fixed at capture: the chunk lengths ``q_lens``, ``max_blocks`` (table
+    width) and ``max_ctx`` (upper bound on any sequence's context). Varying
+    per replay: token ids, start positions, block tables.
+    """
+
+    def __init__(self, model: PagedCausalLM, q_lens: list[int], max_blocks: int, max_ctx: int,
+                 start_pos: list[int], block_tables: list[list[int]], input_ids=None):
+        self.m = model
+        self.q_lens = list(q_lens)
+        self.B = len(q_lens)
+        self.T = int(sum(q_lens))
+        self.max_blocks = max_blocks
+        self.max_ctx = max_ctx
+        dev = model.device
+        buf, B, mb, ctx = pack_metadata(q_lens, start_pos, block_tables, model.block_size, model.num_blocks,
+                                        max_blocks)
+        self.meta_dev = torch.from_numpy(buf).to(dev)
+        self.meta_host = torch.empty(buf.shape, dtype=torch.int32, pin_memory=True)
+        self.ids_dev = torch.zeros(self.T, dtype=torch.int64, device=dev)
+        self.ids_host = torch.empty(self.T, dtype=torch.int64, pin_memory=True)
+        self.tok_host = torch.empty(self.B, dtype=torch.int32, pin_memory=True)
+        if input_ids is not None:
+            self.ids_dev.copy_(torch.as_tensor(np.asarray(input_ids, np.int64)))
+        Bn = self.B
+        self.meta = StepMeta(self.meta_dev[2 * Bn + 1:].view(Bn, mb), self.meta_dev[:Bn + 1],
+                             self.meta_dev[Bn + 1:2 * Bn + 1], self.q_lens, [max_ctx] * Bn)
+        self.last = (self.meta_dev[1:Bn + 1].to(torch.int64) - 1)
+        self.launches_per_replay = 0
+        self.graph = None
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up: sizes the workspaces, loads kernels
+                self._body()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        before = _lib.launch_count()
+        with torch.cuda.graph(self.graph):
+            self.logits, self.tokens = self._body()
+        self.launches_per_replay = _lib.launch_count() - before
+
+    def _body(self):
+        last = self.meta_dev[1:self.B + 1].to(torch.int64) - 1
+        logits = self.m._forward(self.ids_dev, self.meta, last)
+        return logits, self.m.argmax(logits)
+
+    def replay(self) -> None:
+        """Re-run the captured step on the current device buffers."""
+        self.graph.replay()
+
+    def set_inputs(self, input_ids, start_pos: list[int], block_tables: list[list[int]]) -> None:
+        """Host inputs -> pinned staging -> device buffers (async copies on
+        the current stream). Validates like forward_batch."""
+        buf, B, mb, ctx = pack_metadata(self.q_lens, start_pos, block_tables, self.m.block_size, self.m.num_blocks,
+                                        self.max_blocks)
+        if max(ctx) > self.max_ctx:
+            raise IndexError(f"context {max(ctx)} exceeds the captured bound {self.max_ctx}")
+        self.meta_host.numpy()[:] = buf
+        self.ids_host.numpy()[:] = np.asarray(input_ids, np.int64).reshape(-1)
+        self.meta_dev.copy_(self.meta_host, non_blocking=True)
+        self.ids_dev.copy_(self.ids_host, non_blocking=True)
+
+    def run(self, input_ids, start_pos: list[int], block_tables: list[list[int]]) -> np.ndarray:
+        """One step end to end: host inputs in, host next-token ids out."""
+        self.set_inputs(input_ids, start_pos, block_tables)
+        self.graph.replay()
+        self.tok_host.copy_(self.tokens, non_blocking=True)
+        torch.cuda.current_stream(self.m.device).synchronize()
+        return self.tok_host.numpy().copy()
+
+    @property
+    def h2d_bytes(self) -> int:
+        return self.meta_host.numel() * 4 + self.ids_host.numel() * 8
+
+    @property
+    def d2h_bytes(self) -> int:
+        return self.tok_host.numel() * 4

@@ -1,0 +1,155 @@
+"""Drop-in for the reference's engine/quantization.py with a fused W8A16 kernel.
+
+``QuantizedWeight`` keeps the reference's attributes (``q`` int8 (N, K),
+``scale`` float32 (N, 1), ``dtype``, ``get()``, ``to()``, ``storage_bytes``)
+so loaders and tests are unchanged, and adds ``linear(x, bias, residual)``:
+y = x @ (q * scale).T + bias (+ residual) computed by the sm_100a kernel
+without ever materialising the dequantized weight (the reference
+re-dequantizes the whole weight on every ``get()``,
+engine/quantization.py:40-41).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _cuda_device(t: torch.Tensor) -> torch.device:
+    if t.is_cuda:
+        return t.device
+    if not torch.cuda.is_available():
+        raise RuntimeError("pageserve_b200 quantizes on the GPU (no CPU fallback); no CUDA device is available")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def quantize_per_channel(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """engine/quantization.py:16-23, bit-exact, computed on the GPU:
+    scale = max(absmax_k, 1e-8) / 127 (float32, (N, 1)),
+    q = clamp(round_half_even(w / scale), -127, 127) int8 (N, K).
+    Results live on the weight's CUDA device (a CPU weight is moved to the
+    current CUDA device first)."""
+    dev = _cuda_device(weight)
+    w = weight.to(dev).contiguous()
+    if w.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        w = w.float()
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=dev)
+    scale = torch.empty((N, 1), dtype=torch.float32, device=dev)
+    _lib.check(_lib.load().ps_quantize_per_channel(q.data_ptr(), scale.data_ptr(), w.data_ptr(),
+                                                   _lib.dtype_code(w.dtype), N, K, _lib.stream_ptr(dev)),
+               "quantize_per_channel")
+    return q, scale
+
+
+def dequantize(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """engine/quantization.py:26-27 (materialises the weight; the fused
+    kernel path never calls this)."""
+    return (q.to(torch.float32) * scale).to(dtype)
+
+
+class LinearWorkspace:
+    """Grow-only scratch buffer for split-K partial sums."""
+
+    def __init__(self):
+        self.buf: torch.Tensor | None = None
+
+    def get(self, nbytes: int, device) -> torch.Tensor | None:
+        if nbytes == 0:
+            return None
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        return self.buf
+
+
+_default_ws: dict[torch.device, LinearWorkspace] = {}
+
+
+def w8a16_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 workspace: LinearWorkspace | None = None) -> torch.Tensor:
+    """y = x @ (q * scale).T + bias (+ residual): F.linear(x, QuantizedWeight.get(), bias)
+    of engine/model.py:168-190, fused. x (..., K) bf16/f16/f32 on CUDA."""
+    _lib.require_cuda(x, q, scale, bias, residual)
+    N, K = q.shape
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    if residual is not None:
+        residual = residual.reshape(M, N).contiguous()
+    if bias is not None:
+        bias = bias.to(x.dtype).contiguous()
+    lib = _lib.load()
+    ws_bytes = lib.ps_w8a16_linear_workspace_size(M, N, K)
+    if workspace is None:
+        workspace = _default_ws.setdefault(x.device, LinearWorkspace())
+    buf = workspace.get(ws_bytes, x.device)
+    _lib.check(lib.ps_w8a16_linear(out.data_ptr(), x2.data_ptr(), q.data_ptr(), scale.data_ptr(), _lib.ptr(bias),
+                                   _lib.ptr(residual), M, N, K, _lib.dtype_code(x.dtype), _lib.ptr(buf), ws_bytes,
+                                   _lib.stream_ptr(x.device)), "w8a16_linear")
+    return out
+
+
+def linear16(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+             residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+             workspace: LinearWorkspace | None = None) -> torch.Tensor:
+    """F.linear(x, w, bias) with a bf16/f16 weight (the unquantized lm_head,
+    engine/model.py:193)."""
+    _lib.require_cuda(x, w, bias, residual)
+    N, K = w.shape
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    if residual is not None:
+        residual = residual.reshape(M, N).contiguous()
+    lib = _lib.load()
+    ws_bytes = lib.ps_w8a16_linear_workspace_size(M, N, K)
+    if workspace is None:
+        workspace = _default_ws.setdefault(x.device, LinearWorkspace())
+    buf = workspace.get(ws_bytes, x.device)
+    _lib.check(lib.ps_linear(out.data_ptr(), x2.data_ptr(), w.data_ptr(), _lib.ptr(bias), _lib.ptr(residual), M, N,
+                             K, _lib.dtype_code(x.dtype), _lib.ptr(buf), ws_bytes, _lib.stream_ptr(x.device)),
+               "linear")
+    return out
+
+
+class QuantizedWeight:
+    """engine/quantization.py:30-50, same attributes; ``linear`` runs the
+    fused W8A16 kernel."""
+
+    def __init__(self, weight: torch.Tensor):
+        self.dtype = weight.dtype
+        self.q, self.scale = quantize_per_channel(weight)
+
+    @classmethod
+    def from_quantized(cls, q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> "QuantizedWeight":
+        obj = cls.__new__(cls)
+        obj.dtype = dtype
+        obj.q = q.contiguous()
+        obj.scale = scale.reshape(-1, 1).to(torch.float32).contiguous()
+        return obj
+
+    def get(self) -> torch.Tensor:
+        return dequantize(self.q, self.scale, self.dtype)
+
+    def to(self, device) -> "QuantizedWeight":
+        self.q = self.q.to(device)
+        self.scale = self.scale.to(device)
+        return self
+
+    @property
+    def storage_bytes(self) -> int:
+        return self.q.numel() * self.q.element_size() + self.scale.numel() * self.scale.element_size()
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return tuple(self.q.shape)
+
+    def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, workspace: LinearWorkspace | None = None) -> torch.Tensor:
+        return w8a16_linear(x, self.q, self.scale, bias, residual, out, workspace)
