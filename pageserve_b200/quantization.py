@@ -50,7 +50,10 @@ def dequantize(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torc
 
 
 class LinearWorkspace:
-    """Grow-only scratch buffer for split-K partial sums."""
+    """Grow-only scratch buffer for the split-K reduction of the tensor-core
+    linear: arrival counters and float32 partial sums. It must start zeroed;
+    every kernel call leaves the part it used zeroed again, so one buffer is
+    reused by all the linears of a step (calls on one stream only)."""
 
     def __init__(self):
         self.buf: torch.Tensor | None = None
@@ -59,7 +62,7 @@ class LinearWorkspace:
         if nbytes == 0:
             return None
         if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         return self.buf
 
 

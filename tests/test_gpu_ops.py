@@ -282,10 +282,11 @@ def test_fused_rope_qkv_write_kv(dev):
     kc = torch.zeros((NB, bs, Hkv, D), device=dev, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
     qkv_d = _bf16(qkv, dev)
+    pos_d = torch.from_numpy(pos).to(dev)      # keep the device buffers alive
+    slots_d = torch.from_numpy(slots).to(dev)  # until the kernel has run
     _lib.check(_lib.load().ps_rope_qkv_write_kv(
-        q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), qkv_d.data_ptr(), torch.from_numpy(pos).to(dev).data_ptr(),
-        torch.from_numpy(slots).to(dev).data_ptr(), cos.data_ptr(), sin.data_ptr(), 64, T, Hq, Hkv, D, NB * bs,
-        _lib.PS_BF16, _lib.stream_ptr()), "rope")
+        q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), qkv_d.data_ptr(), pos_d.data_ptr(), slots_d.data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), 64, T, Hq, Hkv, D, NB * bs, _lib.PS_BF16, _lib.stream_ptr()), "rope")
     torch.cuda.synchronize()
     ocos, osin = ops.build_rope_cache(64, D, 1.0e6)
     x = ops.round_bf16(qkv)
