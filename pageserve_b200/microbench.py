@@ -1,0 +1,157 @@
+"""Kernel microbenchmarks (BASELINE configs 2 and 3) and small profiling cases.
+
+    python -m pageserve_b200.microbench linear --M 576 --N 22016 --K 2048
+    python -m pageserve_b200.microbench sweep          # config 3: W8A16 sweep
+    python -m pageserve_b200.microbench attn           # config 2: paged decode attention
+
+Timing: CUDA events on the current stream after warm-up; the weight (or KV
+cache) is replicated over enough copies that the rotation exceeds the 126 MB
+L2, so every launch streams from HBM. Prints one JSON object per case.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import sys
+
+import numpy as np
+import torch
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def _peaks():
+    import json as _j
+    from pathlib import Path
+    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = _j.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"]
+    return 6650.0, 1590.0
+
+
+def _time(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3):
+    from .quantization import LinearWorkspace, linear16, w8a16_linear
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    wbytes = N * K * (2 if bf16_weight else 1)
+    copies = max(1, math.ceil(2 * L2_BYTES / wbytes)) if iters > 1 else 1
+    if bf16_weight:
+        ws = [torch.randn(N, K, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(copies)]
+    else:
+        ws = [torch.randint(-127, 128, (N, K), device=dev, generator=g, dtype=torch.int8) for _ in range(copies)]
+    scale = torch.empty(N, 1, device=dev).uniform_(1e-3, 1e-2, generator=g)
+    x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    wsp = LinearWorkspace()
+    ctr = [0]
+
+    def f():
+        w = ws[ctr[0] % copies]
+        ctr[0] += 1
+        if bf16_weight:
+            linear16(x, w, out=out, workspace=wsp)
+        else:
+            w8a16_linear(x, w, scale, out=out, workspace=wsp)
+    ms = _time(f, iters, warmup)
+    hbm, tf = _peaks()
+    flops = 2.0 * M * N * K
+    byts = wbytes + (0 if bf16_weight else 4 * N) + 2 * M * K + 2 * M * N
+    bound = "tensor" if flops / (tf * 1e12) > byts / (hbm * 1e9) else "hbm"
+    ach_tf = flops / ms / 1e9
+    ach_gb = byts / ms / 1e6
+    return {"case": "linear", "M": M, "N": N, "K": K, "weight": "bf16" if bf16_weight else "int8", "us": ms * 1e3,
+            "tflops": ach_tf, "gbs": ach_gb, "bound": bound,
+            "frac": (ach_tf / tf) if bound == "tensor" else (ach_gb / hbm),
+            "ideal_us": max(flops / (tf * 1e12), byts / (hbm * 1e9)) * 1e6}
+
+
+def bench_attn(B=64, lo=512, hi=4096, Hq=16, Hkv=2, D=128, bs=16, pool=20000, iters=20, seed=0, warmup=3):
+    """paged decode attention, bf16, ctx ~ U[lo, hi],
+    block tables a random permutation of a 20k-block pool."""
+    from .paged_attention import AttentionWorkspace, paged_attention
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(lo, hi + 1, (B,), generator=g)
+    nblk = [(int(c) + bs - 1) // bs for c in ctx]
+    assert sum(nblk) <= pool
+    perm = torch.randperm(pool, generator=g)
+    mb = max(nblk)
+    tab = torch.full((B, mb), -1, dtype=torch.int32)
+    at = 0
+    for b, n in enumerate(nblk):
+        tab[b, :n] = perm[at:at + n].to(torch.int32)
+        at += n
+    kv_bytes = pool * bs * Hkv * D * 2
+    copies = max(1, math.ceil(2 * L2_BYTES / (2 * kv_bytes))) if iters > 1 else 1
+    gd = torch.Generator(device=dev)
+    gd.manual_seed(seed)
+    caches = [(torch.randn(pool, bs, Hkv, D, device=dev, generator=gd, dtype=torch.bfloat16),
+               torch.randn(pool, bs, Hkv, D, device=dev, generator=gd, dtype=torch.bfloat16)) for _ in range(copies)]
+    q = torch.randn(B, Hq, D, device=dev, generator=gd, dtype=torch.bfloat16)
+    tab = tab.to(dev)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    sp = (ctx - 1).to(torch.int32).to(dev)
+    out = torch.empty_like(q)
+    aws = AttentionWorkspace()
+    ctr = [0]
+
+    def f():
+        kc, vc = caches[ctr[0] % copies]
+        ctr[0] += 1
+        paged_attention(q, kc, vc, tab, cu, sp, 1, int(ctx.max()), out=out, workspace=aws)
+    ms = _time(f, iters, warmup)
+    hbm, _ = _peaks()
+    tot = int(ctx.sum())
+    byts = tot * Hkv * D * 2 * 2 + 2 * B * Hq * D * 2 + 4 * sum(nblk)
+    return {"case": "attn_decode", "B": B, "ctx_sum": tot, "us": ms * 1e3, "bytes": byts, "gbs": byts / ms / 1e6,
+            "frac": byts / ms / 1e6 / hbm, "ideal_us": byts / (hbm * 1e9) * 1e6}
+
+
+SWEEP_NK = [(2560, 2048), (2048, 2048), (22016, 2048), (2048, 11008)]
+SWEEP_M = [1, 8, 64, 256, 2048]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["linear", "sweep", "attn"])
+    ap.add_argument("--M", type=int, default=576)
+    ap.add_argument("--N", type=int, default=22016)
+    ap.add_argument("--K", type=int, default=2048)
+    ap.add_argument("--bf16-weight", action="store_true")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    torch.cuda.init()
+    if a.what == "linear":
+        print(json.dumps(bench_linear(a.M, a.N, a.K, a.iters, bf16_weight=a.bf16_weight, warmup=a.warmup)))
+    elif a.what == "sweep":
+        for n, k in SWEEP_NK:
+            for m in SWEEP_M:
+                print(json.dumps(bench_linear(m, n, k, a.iters, warmup=a.warmup)), flush=True)
+    else:
+        print(json.dumps(bench_attn(iters=a.iters, warmup=a.warmup)))
+    from . import _lib
+    _lib.raise_on_device_error()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
