@@ -110,6 +110,26 @@ PS_API int ps_paged_attention(void* out_dev, const void* q_dev, const void* k_ca
                        int num_blocks, int block_size, int num_q_heads, int num_kv_heads, int head_dim,
                        int dtype, void* workspace_dev, size_t workspace_bytes, ps_stream_t stream);
 
+/* Allocation-free form of ps_paged_attention. No counterpart in the
+ * reference: it serves callers that cannot call cudaMalloc (a plugin whose
+ * host engine owns all device memory through its own pool, or a latency-
+ * critical path where cudaMalloc's implicit synchronisation is not allowed).
+ * Same inputs, outputs and semantics as ps_paged_attention, without the
+ * workspace arguments: the split-context scratch is a static device array of
+ * PS_ATTN_NOALLOC_SCRATCH_BYTES (16 MiB) that every GPU loading this library
+ * holds until exit. A batch whose scratch need exceeds it is rejected with
+ * PS_ERR_INVALID before any launch. The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress); make it before any stream capture.
+ * Calls that overlap on the GPU share the array and race. Device-side range
+ * errors skip the access but are not recorded in the status word. */
+#define PS_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
+PS_API int ps_paged_attention_noalloc(void* out_dev, const void* q_dev, const void* k_cache_dev,
+                                      const void* v_cache_dev, const int32_t* block_tables_dev,
+                                      int max_blocks_per_seq, const int32_t* cu_q_dev, const int32_t* start_pos_dev,
+                                      int num_seqs, int total_q, int max_q_len, int max_ctx, int num_blocks,
+                                      int block_size, int num_q_heads, int num_kv_heads, int head_dim, int dtype,
+                                      ps_stream_t stream);
+
 /* ------------------------------------------------ (a6-a7) W8A16 linear */
 
 /* engine/quantization.py:16-23 (quantize_per_channel) on the device:

@@ -38,6 +38,8 @@ _SIGNATURES = {
     "ps_paged_attention_workspace_size": (c_size_t, [_I, _I, _I, _I, _I, _I]),
     "ps_paged_attention": (c_int, [_P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P,
                                    c_size_t, _P]),
+    "ps_paged_attention_noalloc": (c_int, [_P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I,
+                                           _P]),
     "ps_quantize_per_channel": (c_int, [_P, _P, _P, _I, _I, _I, _P]),
     "ps_w8a16_linear_workspace_size": (c_size_t, [_I, _I, _I]),
     "ps_w8a16_linear": (c_int, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, c_size_t, _P]),

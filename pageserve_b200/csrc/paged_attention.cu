@@ -18,6 +18,7 @@
 //     key tiles; the causal bound stops each CTA at its last row's position.
 // The kernel is HBM bound: it reads each cached K/V row of the context once.
 #include <cfloat>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -576,3 +577,132 @@ int ps_paged_attention(void* out, const void* q, const void* k_cache, const void
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// ps_paged_attention needs a caller-provided workspace for its split-context
+// partials and lazily cudaMalloc's a per-device status word. Some callers can
+// do neither: a plugin hosted by another serving engine whose device memory
+// is owned entirely by that engine's pool allocator, or a latency-critical
+// path that may not call cudaMalloc (it can synchronise the device). This
+// variant takes the same inputs and outputs but keeps its scratch in the
+// file-scope array below, sized PS_ATTN_NOALLOC_SCRATCH_BYTES; every GPU that
+// loads this library reserves it until the process exits.
+//
+// Its first call on a device looks up the array's device address with
+// cudaGetSymbolAddress (the host-side name of a __device__ array is not a
+// device address); make that first call before any stream capture. All calls
+// on a device share the array: calls that overlap on the GPU (different
+// streams, or threads racing) corrupt each other's partials. Nothing in the
+// array must start at zero: every split writes its partial output and
+// log-sum-exp before the combine kernel reads them, so a previous call's
+// contents are never read. Device-side range errors (a block id outside the
+// pool) skip the access as in ps_paged_attention but are not recorded, since
+// this variant owns no status word.
+namespace {
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[PS_ATTN_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    ps_host::set_error("paged_attention_noalloc: no current device (%s)", cudaGetErrorString(e));
+    return PS_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      ps_host::set_error("paged_attention_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return PS_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PS_OK;
+}
+
+}  // namespace
+
+extern "C" int ps_paged_attention_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* tables, int max_blocks, const int32_t* cu_q,
+                                          const int32_t* start_pos, int num_seqs, int total_q, int max_q_len,
+                                          int max_ctx, int num_blocks, int block_size, int Hq, int Hkv, int D,
+                                          int dtype, ps_stream_t stream) {
+  if (num_seqs <= 0 || total_q < 0 || max_q_len <= 0 || max_ctx < max_q_len || block_size <= 0 ||
+      num_blocks <= 0 || max_blocks <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) {
+    ps_host::set_error("paged_attention_noalloc: invalid sizes (seqs %d, max_q %d, max_ctx %d)", num_seqs,
+                       max_q_len, max_ctx);
+    return PS_ERR_INVALID;
+  }
+  if (max_ctx > max_blocks * block_size) {
+    ps_host::set_error("paged_attention_noalloc: context %d needs %d table entries, table has %d", max_ctx,
+                       (max_ctx + block_size - 1) / block_size, max_blocks);
+    return PS_ERR_INDEX;
+  }
+  if (!out || !q || !k_cache || !v_cache || !tables || !cu_q || !start_pos) {
+    ps_host::set_error("paged_attention_noalloc: null pointer");
+    return PS_ERR_INVALID;
+  }
+  if (!ps_host::aligned(k_cache, 16) || !ps_host::aligned(v_cache, 16) || !ps_host::aligned(q, 4) ||
+      !ps_host::aligned(out, 4)) {
+    ps_host::set_error("paged_attention_noalloc: caches need 16-byte, q/out 4-byte alignment");
+    return PS_ERR_INVALID;
+  }
+  const size_t need = workspace_bytes_for(num_seqs, max_q_len, max_ctx, Hq, Hkv, D);
+  if (need > PS_ATTN_NOALLOC_SCRATCH_BYTES) {
+    ps_host::set_error(
+        "paged_attention_noalloc: this batch needs %zu bytes of split scratch, above the static limit of %zu "
+        "bytes (use ps_paged_attention with a workspace)",
+        need, static_cast<size_t>(PS_ATTN_NOALLOC_SCRATCH_BYTES));
+    return PS_ERR_INVALID;
+  }
+  if (total_q == 0) return PS_OK;
+  AttnParams p{};
+  p.out = out;
+  p.q = q;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.tables = tables;
+  p.cu_q = cu_q;
+  p.start_pos = start_pos;
+  p.status = nullptr;
+  p.max_blocks = max_blocks;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = Hq / Hkv;
+  p.rows_max = max_q_len * Hq;
+  p.max_q_len = max_q_len;
+  p.max_ctx = max_ctx;
+  p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * kLog2e;
+  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, &p.num_splits, &p.split_tokens);
+  if (p.num_splits > 1) {
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != PS_OK) return rc;
+    const size_t rows = static_cast<size_t>(num_seqs) * p.num_splits * p.rows_max;
+    p.o_part = static_cast<float*>(scratch);  // the array is 256-byte aligned
+    p.lse_part = p.o_part + rows * D;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == PS_BF16) {
+    if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s);
+    if (D == 64) return launch<__nv_bfloat16, 64>(p, num_seqs, max_q_len, max_ctx, s);
+  } else if (dtype == PS_F16) {
+    if (D == 128) return launch<__half, 128>(p, num_seqs, max_q_len, max_ctx, s);
+    if (D == 64) return launch<__half, 64>(p, num_seqs, max_q_len, max_ctx, s);
+  } else {
+    ps_host::set_error("paged_attention_noalloc: dtype must be bf16 or f16");
+    return PS_ERR_UNSUPPORTED;
+  }
+  ps_host::set_error("paged_attention_noalloc: head_dim %d unsupported (64, 128)", D);
+  return PS_ERR_UNSUPPORTED;
+}

@@ -1,0 +1,97 @@
+"""The allocation-free paged-attention entry point (ps_paged_attention_noalloc).
+
+It exists for callers that cannot call cudaMalloc — e.g. a plugin whose host
+serving engine owns all device memory through its own pool, or a latency-
+critical path where cudaMalloc's implicit synchronisation is not allowed. It
+keeps its split-context scratch in a static device array instead of a
+caller-provided workspace. These tests call it through the C ABI and check it
+against ps_paged_attention (the entry point with a workspace) on two
+consecutive calls, plus the host-side rejection of batches whose scratch need
+is above the static limit.
+
+This file is named to be collected last, so a stop-at-first-failure run has
+already run every other test; it also passes alone in a fresh process.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 2e-2  # the bf16 tolerance used by the other GPU tests
+NOALLOC_LIMIT = 16 << 20  # PS_ATTN_NOALLOC_SCRATCH_BYTES in include/pageserve_b200.h
+
+
+def rel_err(a, b):
+    a = a.double()
+    b = b.double()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def _batch(seed, B, lo, hi, dev, Hq=16, Hkv=2, D=128, bs=16):
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(lo, hi + 1, size=B)
+    nblk = [(int(c) + bs - 1) // bs for c in ctx]
+    NB = sum(nblk) + 5
+    perm = rng.permutation(NB)
+    mb = max(nblk)
+    tab = np.full((B, mb), -1, np.int32)
+    at = 0
+    for b, n in enumerate(nblk):
+        tab[b, :n] = perm[at:at + n]
+        at += n
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    kc = torch.randn(NB, bs, Hkv, D, device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(NB, bs, Hkv, D, device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(B, Hq, D, device=dev, generator=g, dtype=torch.bfloat16)
+    return dict(q=q, kc=kc, vc=vc, tab=torch.from_numpy(tab).to(dev),
+                cu=torch.arange(B + 1, dtype=torch.int32, device=dev),
+                sp=torch.from_numpy((ctx - 1).astype(np.int32)).to(dev), B=B, mb=mb, max_ctx=int(ctx.max()), NB=NB,
+                bs=bs, Hq=Hq, Hkv=Hkv, D=D)
+
+
+def _args(c, out):
+    return (out.data_ptr(), c["q"].data_ptr(), c["kc"].data_ptr(), c["vc"].data_ptr(), c["tab"].data_ptr(), c["mb"],
+            c["cu"].data_ptr(), c["sp"].data_ptr(), c["B"], c["B"], 1, c["max_ctx"], c["NB"], c["bs"], c["Hq"],
+            c["Hkv"], c["D"])
+
+
+def test_noalloc_attention_matches_workspace_entry_point_twice():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from pageserve_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    stream = _lib.stream_ptr(dev)
+    for call, (seed, B, lo, hi) in enumerate([(1, 16, 600, 2048), (2, 24, 300, 3000)]):
+        c = _batch(seed, B, lo, hi, dev)
+        ws_bytes = lib.ps_paged_attention_workspace_size(B, 1, c["max_ctx"], c["Hq"], c["Hkv"], c["D"])
+        assert 0 < ws_bytes <= NOALLOC_LIMIT, "the case must use split scratch"
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        ref = torch.empty_like(c["q"])
+        got = torch.full_like(c["q"], float("nan"))
+        _lib.check(lib.ps_paged_attention(*_args(c, ref), _lib.PS_BF16, ws.data_ptr(), ws_bytes, stream),
+                   "paged_attention")
+        _lib.check(lib.ps_paged_attention_noalloc(*_args(c, got), _lib.PS_BF16, stream), "paged_attention_noalloc")
+        torch.cuda.synchronize()
+        assert torch.isfinite(got).all(), f"call {call}: unwritten output"
+        assert rel_err(got.float(), ref.float()) < REL_TOL, f"call {call}"
+
+
+def test_noalloc_rejects_batches_above_the_static_scratch():
+    from pageserve_b200 import _lib
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("library not built")
+    lib = _lib.load()
+    # 64 sequences x 2 query tokens x 64 heads at context 4096 need ~16.9 MB of partials
+    need = lib.ps_paged_attention_workspace_size(64, 2, 4096, 64, 8, 128)
+    assert need > NOALLOC_LIMIT
+    fake = 1 << 20  # never dereferenced: the size check runs before any device access
+    rc = lib.ps_paged_attention_noalloc(fake, fake, fake, fake, fake, 256, fake, fake, 64, 128, 2, 4096, 1024, 16,
+                                        64, 8, 128, _lib.PS_BF16, None)
+    assert rc == _lib.PS_ERR_INVALID
+    assert "static limit" in _lib.last_error()
