@@ -150,6 +150,19 @@ PS_API int ps_w8a16_linear(void* y_dev, const void* x_dev, const int8_t* q_dev, 
                     const void* bias_dev, const void* residual_dev, int M, int N, int K, int dtype,
                     void* workspace_dev, size_t workspace_bytes, ps_stream_t stream);
 
+/* The same W8A16 linear on a weight re-tiled once (ps_tile_int8_weight) into
+ * contiguous 8 KB blocks [ceil(N/128)][ceil(K/64)][128][64] (zero padded):
+ * every main-loop weight tile is one contiguous bulk copy instead of 128-256
+ * separate 64-byte rows. Always runs on the tensor cores (bf16/f16). The
+ * reference keeps q row-major (engine/quantization.py:33-34); the tiled copy
+ * is this build's kernel-side layout of the same int8 values. */
+PS_API size_t ps_tiled_int8_weight_bytes(int N, int K);
+PS_API int ps_tile_int8_weight(int8_t* q_tiled_dev, const int8_t* q_dev, int N, int K, ps_stream_t stream);
+PS_API size_t ps_w8a16_linear_tiled_workspace_size(int M, int N, int K);
+PS_API int ps_w8a16_linear_tiled(void* y_dev, const void* x_dev, const int8_t* q_tiled_dev, const float* scale_dev,
+                                 const void* bias_dev, const void* residual_dev, int M, int N, int K, int dtype,
+                                 void* workspace_dev, size_t workspace_bytes, ps_stream_t stream);
+
 /* Plain linear with a 16-bit weight (the unquantized lm_head,
  * engine/model.py:193): y[m,n] = sum_k x[m,k] * w[n,k] (+ bias). */
 PS_API int ps_linear(void* y_dev, const void* x_dev, const void* w_dev, const void* bias_dev, const void* residual_dev,

@@ -43,6 +43,10 @@ _SIGNATURES = {
     "ps_quantize_per_channel": (c_int, [_P, _P, _P, _I, _I, _I, _P]),
     "ps_w8a16_linear_workspace_size": (c_size_t, [_I, _I, _I]),
     "ps_w8a16_linear": (c_int, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, c_size_t, _P]),
+    "ps_tiled_int8_weight_bytes": (c_size_t, [_I, _I]),
+    "ps_tile_int8_weight": (c_int, [_P, _P, _I, _I, _P]),
+    "ps_w8a16_linear_tiled_workspace_size": (c_size_t, [_I, _I, _I]),
+    "ps_w8a16_linear_tiled": (c_int, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, c_size_t, _P]),
     "ps_linear": (c_int, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, c_size_t, _P]),
     "ps_silu_mul": (c_int, [_P, _P, _I, _I, _I, _P]),
     "ps_rmsnorm": (c_int, [_P, _P, _P, _P, _P, c_float, _I, _I, _I, _P]),

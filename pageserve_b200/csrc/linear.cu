@@ -1,10 +1,20 @@
 // C entry points of the linear kernels: pick the CUDA-core streaming kernel
 // for small M and the tcgen05 tensor-core kernel above it.
+#include <cstdlib>
+
 #include "linear.cuh"
 
 namespace {
 
-constexpr int kSimtMaxM = 16;
+// Largest M served by the CUDA-core streaming kernel; above it the tcgen05
+// kernel runs. PS_SIMT_MAX_M overrides it (tuning).
+int simt_max_m() {
+  static const int v = [] {
+    const char* e = std::getenv("PS_SIMT_MAX_M");
+    return e ? std::atoi(e) : 1;
+  }();
+  return v;
+}
 
 int linear_any(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
                const void* resid, int M, int N, int K, int dtype, void* ws, size_t ws_bytes, ps_stream_t stream,
@@ -24,7 +34,7 @@ int linear_any(void* y, const void* x, const void* w, int wdtype, const float* s
     return PS_ERR_INVALID;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (M > kSimtMaxM && dtype != PS_F32) {
+  if (M > simt_max_m() && dtype != PS_F32) {
     const int rc = ps_host::linear_tc(y, x, w, wdtype, scale, bias, resid, M, N, K, dtype, ws, ws_bytes, s);
     if (rc != PS_ERR_UNSUPPORTED) return rc;
   }
@@ -36,7 +46,7 @@ int linear_any(void* y, const void* x, const void* w, int wdtype, const float* s
 extern "C" {
 
 size_t ps_w8a16_linear_workspace_size(int M, int N, int K) {
-  return M > kSimtMaxM ? ps_host::linear_tc_workspace(M, N, K) : 0;
+  return M > simt_max_m() ? ps_host::linear_tc_workspace(M, N, K) : 0;
 }
 
 int ps_w8a16_linear(void* y, const void* x, const int8_t* q, const float* scale, const void* bias,
@@ -48,6 +58,39 @@ int ps_w8a16_linear(void* y, const void* x, const int8_t* q, const float* scale,
   }
   return linear_any(y, x, q, PS_I8, scale, bias, resid, M, N, K, dtype, ws, ws_bytes, stream, "w8a16_linear");
 }
+
+size_t ps_tiled_int8_weight_bytes(int N, int K) { return N > 0 && K > 0 ? ps_host::tiled_int8_bytes(N, K) : 0; }
+
+int ps_tile_int8_weight(int8_t* dst, const int8_t* q, int N, int K, ps_stream_t stream) {
+  if (N <= 0 || K <= 0 || !dst || !q || !ps_host::aligned(dst, 16)) {
+    ps_host::set_error("tile_int8_weight: invalid arguments");
+    return PS_ERR_INVALID;
+  }
+  return ps_host::tile_int8(dst, q, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ps_w8a16_linear_tiled(void* y, const void* x, const int8_t* q_tiled, const float* scale, const void* bias,
+                          const void* resid, int M, int N, int K, int dtype, void* ws, size_t ws_bytes,
+                          ps_stream_t stream) {
+  if (M < 0 || N <= 0 || K <= 0 || !y || !x || !q_tiled || !scale) {
+    ps_host::set_error("w8a16_linear_tiled: invalid arguments (M=%d N=%d K=%d)", M, N, K);
+    return PS_ERR_INVALID;
+  }
+  if (M == 0) return PS_OK;
+  if (dtype != PS_BF16 && dtype != PS_F16) {
+    ps_host::set_error("w8a16_linear_tiled: dtype must be bf16 or f16");
+    return PS_ERR_UNSUPPORTED;
+  }
+  if (!ps_host::aligned(y, 16) || !ps_host::aligned(x, 16) || !ps_host::aligned(q_tiled, 16) ||
+      !ps_host::aligned(scale, 16) || !ps_host::aligned(resid, 16) || !ps_host::aligned(bias, 16) || K % 16 != 0) {
+    ps_host::set_error("w8a16_linear_tiled: tensors must be 16-byte aligned and K a multiple of 16");
+    return PS_ERR_INVALID;
+  }
+  return ps_host::linear_tc(y, x, q_tiled, PS_I8, scale, bias, resid, M, N, K, dtype, ws, ws_bytes,
+                            reinterpret_cast<cudaStream_t>(stream), q_tiled);
+}
+
+size_t ps_w8a16_linear_tiled_workspace_size(int M, int N, int K) { return ps_host::linear_tc_workspace(M, N, K); }
 
 int ps_linear(void* y, const void* x, const void* w, const void* bias, const void* resid, int M, int N, int K,
               int dtype, void* ws, size_t ws_bytes, ps_stream_t stream) {

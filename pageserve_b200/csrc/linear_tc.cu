@@ -4,28 +4,40 @@
 // reference).
 //
 // Orientation ("swap AB"): the MMA's 128-row M dimension walks the weight's
-// output channels and its N dimension walks the tokens, so one CTA owns a
-// 128-channel weight slab for a tile of up to 256 tokens and every weight byte
-// is fetched and widened once per token tile. Decode batches (tens of tokens)
-// stream the int8 weight at HBM speed; prefill tiles run tensor-bound.
+// output channels and its N dimension walks the tokens, so a CTA owns a slab
+// of NSUB*128 output channels for a tile of BM (<= 256) tokens and every
+// weight byte is fetched and widened once per token tile. With NSUB = 2 two
+// M=128 MMAs share each activation tile (half the activation traffic per
+// flop); decode-sized batches use NSUB = 1 for more CTAs.
 //
-// Roles (192 threads):
-//   warp 0        TMA producer: int8 weight tile (128 x 64 B) and the bf16
-//                 activation tile (BM x 128 B, 128B-swizzled) per stage
-//   warp 1        TMEM allocator; one elected lane issues tcgen05.mma
-//                 (M=128, N=BM, K=16) x 4 per stage, commits to mbarriers
-//   warps 2..5    widen int8 -> bf16 (exact: |q| <= 127) into the
-//                 128B-swizzled K-major UMMA operand layout, then run the
-//                 epilogue from TMEM (scale, bias, residual, store / split-K
-//                 reduction)
-// The per-channel scale is applied once per output after accumulation, so
-// the tensor-core operand is the exact integer weight.
+// Roles (352 threads), each ring with its own full/empty mbarrier pair:
+//   warp 0      weight producer: TMA of the int8 tile (NSUB*128 x 64 B) into
+//               a deep ring (or the bf16 tile straight into the operand ring)
+//   warp 1      TMEM allocator; one elected lane issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BM, K=16),
+//               NSUB x 4 per k-tile, and commits to the rings' empty barriers
+//   warp 2      activation producer: TMA of the bf16 tile (BM x 128 B,
+//               128B swizzle) into its ring
+//   warps 3..10 widen int8 -> bf16 (exact: |q| <= 127) into a 2-deep ring in
+//               the 128B-swizzled K-major UMMA layout, running up to two
+//               k-tiles ahead of the MMA (two warps per SM sub-partition: the
+//               widening is latency bound); then the epilogue from TMEM
+//               (tcgen05.ld 32x32b; warp w reads lane quarter w%4, half of
+//               the columns), transposed through shared memory so each lane
+//               stores 16 consecutive outputs (scale, bias, residual)
+// The weight stream runs ahead independently of the MMA, so HBM latency is
+// hidden by the weight ring depth rather than by the MMA's commit chain.
+// Small-N shapes split K across CTAs: each split stores float32 partials
+// (no atomics) and a separate wide kernel reduces them and applies the
+// epilogue (a single CTA reducing a whole tile was latency bound).
 //
 // Every mbarrier wait is bounded (about a second of clock64 cycles): on
 // timeout the kernel records kErrTimeout in the status word, stops issuing
 // work, releases its TMEM and returns.
 #include <cudaTypedefs.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "linear.cuh"
@@ -34,10 +46,26 @@ namespace {
 
 using namespace ps;
 
-constexpr int kThreads = 192;
-constexpr int kBN = 128;  // weight rows per CTA (MMA M)
-constexpr int kBK = 64;   // K elements per stage (128 bytes of bf16 = one swizzle atom row)
+constexpr int kThreads = 352;
+constexpr int kDeqWarps = 8;
+constexpr int kBK = 64;  // K elements per k-tile (128 bytes of bf16 = one swizzle row)
 constexpr long long kWaitCycles = 2000000000LL;
+constexpr int kSmemBudget = 216 * 1024;
+
+// Pipeline event timestamps of CTA (0,0,0) for latency analysis; compiled
+// only with -DPS_TRACE (never in the shipped library).
+#ifdef PS_TRACE
+__device__ unsigned long long g_tc_trace[4096];
+#define PS_TC_TRACE(slot, cond)                                                    \
+  do {                                                                             \
+    if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)           \
+      g_tc_trace[(slot)] = clock64();                                              \
+  } while (0)
+#else
+#define PS_TC_TRACE(slot, cond) \
+  do {                          \
+  } while (0)
+#endif
 
 // ------------------------------------------------------------- PTX bits --
 PS_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
@@ -61,19 +89,25 @@ PS_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait. Returns false (and raises the CTA abort flag) on timeout or
-// when another role already aborted.
-PS_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+// Bounded wait by every lane of a warp; the result is warp-uniform. Returns
+// false (and raises the CTA abort flag) on timeout or when another role
+// already aborted.
+PS_DEVICE bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  bool ok = true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (*abort_flag) return false;
+    if (*abort_flag) {
+      ok = false;
+      break;
+    }
     if (clock64() - t0 > kWaitCycles) {
       *abort_flag = 1;
       record_error(status, kErrTimeout);
-      return false;
+      ok = false;
+      break;
     }
   }
-  return true;
+  return __all_sync(0xffffffffu, ok);
 }
 
 PS_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
@@ -82,6 +116,13 @@ PS_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, i
           dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
+}
+
+// Contiguous global -> shared bulk copy (16-byte aligned, size multiple of 16).
+PS_DEVICE void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 
 PS_DEVICE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -141,8 +182,7 @@ PS_DEVICE void widen16_bf16(const uint4& in, uint4& lo, uint4& hi) {
     const uint32_t sign = w[j] & 0x80808080u;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      // bytes 2h, 2h+1 -> bf16 pair {0x43 : byte}
-      const uint32_t sel = h ? 0x4342u : 0x4140u;
+      const uint32_t sel = h ? 0x4342u : 0x4140u;  // bytes (2h, 2h+1) -> two bf16 {0x43 : byte}
       const uint32_t a = __byte_perm(low7, 0x43434343u, sel);
       const uint32_t b = __byte_perm(sign, 0x43434343u, sel);
       uint32_t r;
@@ -154,7 +194,7 @@ PS_DEVICE void widen16_bf16(const uint4& in, uint4& lo, uint4& hi) {
   hi = make_uint4(out[4], out[5], out[6], out[7]);
 }
 PS_DEVICE void widen16_f16(const uint4& in, uint4& lo, uint4& hi) {
-  // f16: 0x6400 | byte = 1024 + byte; subtract 1024 + 128 after flipping the sign bit.
+  // f16: 0x64:byte = 1024 + byte; flip the sign bit first, subtract 1024 + 128.
   const uint32_t w[4] = {in.x ^ 0x80808080u, in.y ^ 0x80808080u, in.z ^ 0x80808080u, in.w ^ 0x80808080u};
   uint32_t out[8];
   const uint32_t bias = 0x64806480u;  // 1152.0 in both halves
@@ -172,12 +212,13 @@ PS_DEVICE void widen16_f16(const uint4& in, uint4& lo, uint4& hi) {
 }
 
 struct TcParams {
+  const int8_t* wt;  // int8 weight pre-tiled in 8 KB blocks [N/128][K/64][128][64] (or null: row-major via TMA)
+  int n_blocks;      // ceil(N / 128)
   void* y;
   const float* scale;
   const void* bias;
   const void* resid;
-  float* ws;        // split-K fp32 partial sums [M][N] (kept zeroed)
-  int* counters;    // split-K arrival counters [m_tiles][n_tiles] (kept zeroed)
+  float* part;      // split-K float32 partials [splits][M][N]
   int* status;
   int M, N, K;
   int k_tiles;      // total K tiles of 64
@@ -185,123 +226,181 @@ struct TcParams {
   int splits;
 };
 
-template <typename T, bool kInt8, int BM, int STAGES>
-struct Smem {
-  static constexpr int kA = kBN * kBK * 2;       // bf16 weight operand
-  static constexpr int kW8 = kInt8 ? kBN * kBK : 0;  // raw int8 weight
-  static constexpr int kX = BM * kBK * 2;        // activation operand
-  static constexpr int kStage = kA + kW8 + kX;
-  static constexpr int kBytes = STAGES * kStage + 1024 /*align*/ + 256 /*barriers*/;
+// Shared-memory plan of one configuration.
+template <bool kInt8, int NSUB, int BM>
+struct Cfg {
+  static constexpr int kBN = 128 * NSUB;
+  static constexpr int kW = kInt8 ? kBN * kBK : kBN * kBK * 2;  // weight ring stage
+  static constexpr int kX = BM * kBK * 2;                        // activation ring stage
+  static constexpr int kA = kInt8 ? kBN * kBK * 2 : 0;           // widened operand stage
+  static constexpr int kAS = kInt8 ? 2 : 0;                      // widened operand stages
+  static constexpr int kEpi = kDeqWarps * 16 * 32 * 4;           // per-warp transpose tiles
+  static constexpr int kRX0 = (96 * 1024) / kX;
+  static constexpr int kRX = kRX0 < 2 ? 2 : (kRX0 > 8 ? 8 : kRX0);
+  static constexpr int kRW0 = (kSmemBudget - kAS * kA - kRX * kX) / kW;
+  static constexpr int kRW = kRW0 < 2 ? 2 : (kRW0 > 8 ? 8 : kRW0);
+  // layout (1024-aligned rings first): A | W | X | barriers. The epilogue's
+  // transpose tiles reuse the weight ring, idle once the main loop is done.
+  static constexpr int kOffA = 0;
+  static constexpr int kOffW = kOffA + kAS * kA;
+  static constexpr int kOffX = kOffW + kRW * kW;
+  static constexpr int kOffEpi = kOffW;
+  static constexpr int kOffBar = kOffX + kRX * kX;
+  static constexpr int kBytes = kOffBar + 512 + 1024;
+  static constexpr int kTmemCols = NSUB * BM <= 32 ? 32 : (NSUB * BM <= 64 ? 64 : (NSUB * BM <= 128 ? 128 :
+                                   (NSUB * BM <= 256 ? 256 : 512)));
+  static_assert(kBytes <= 227 * 1024, "shared memory plan too large");
+  static_assert(kRW * kW >= kEpi, "epilogue tiles alias the weight ring");
+  static_assert(NSUB * BM <= 512, "TMEM columns");
+  static_assert(kW % 1024 == 0 && kX % 1024 == 0 && kA % 1024 == 0, "1024-byte aligned stages");
 };
 
-template <typename T, bool kInt8, int BM, int STAGES>
+template <typename T, bool kInt8, int NSUB, int BM>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                      const TcParams p) {
-  using S = Smem<T, kInt8, BM, STAGES>;
+  using C = Cfg<kInt8, NSUB, BM>;
+  constexpr int RW = C::kRW, RX = C::kRX;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
-  // stage s: [A bf16 | X bf16 | W int8]; A and X are 1024-aligned
-  auto a_addr = [&](int s) { return base + s * S::kStage; };
-  auto x_addr = [&](int s) { return base + s * S::kStage + S::kA; };
-  auto w8_addr = [&](int s) { return base + s * S::kStage + S::kA + S::kX; };
-  const uint32_t bars = base + STAGES * S::kStage;
-  auto tma_full = [&](int s) { return bars + 8 * s; };
-  auto deq_full = [&](int s) { return bars + 8 * (STAGES + s); };
-  auto mma_done = [&](int s) { return bars + 8 * (2 * STAGES + s); };
-  const uint32_t acc_full = bars + 8 * (3 * STAGES);
-  unsigned char* misc = gbase + STAGES * S::kStage + 8 * (3 * STAGES + 1);
+  auto a_addr = [&](int s) { return base + C::kOffA + s * C::kA; };
+  auto w_addr = [&](int s) { return base + C::kOffW + s * C::kW; };
+  auto x_addr = [&](int s) { return base + C::kOffX + s * C::kX; };
+  const uint32_t bars = base + C::kOffBar;
+  auto w_full = [&](int s) { return bars + 8 * s; };
+  auto w_empty = [&](int s) { return bars + 8 * (8 + s); };
+  auto x_full = [&](int s) { return bars + 8 * (16 + s); };
+  auto x_empty = [&](int s) { return bars + 8 * (24 + s); };
+  auto a_full = [&](int s) { return bars + 8 * (32 + s); };
+  auto a_empty = [&](int s) { return bars + 8 * (34 + s); };
+  const uint32_t acc_full = bars + 8 * 36;
+  unsigned char* misc = gbase + C::kOffBar + 8 * 40;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 4);
-  int* last_flag = reinterpret_cast<int*>(misc + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN;
+  const int n0 = blockIdx.x * C::kBN;
   const int m0 = blockIdx.y * BM;
   const int split = blockIdx.z;
   const int kt0 = split * p.k_tiles_per_split;
   const int kt1 = min(p.k_tiles, kt0 + p.k_tiles_per_split);
   const int nkt = kt1 - kt0;
-  constexpr int kTmemCols = BM <= 32 ? 32 : (BM <= 64 ? 64 : (BM <= 128 ? 128 : 256));
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    *last_flag = 0;
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(tma_full(s), 1);
-      mbar_init(deq_full(s), kInt8 ? 4 : 1);
-      mbar_init(mma_done(s), 1);
+    for (int s = 0; s < RW; ++s) {
+      mbar_init(w_full(s), 1);
+      mbar_init(w_empty(s), kInt8 ? kDeqWarps : 1);
+    }
+    for (int s = 0; s < RX; ++s) {
+      mbar_init(x_full(s), 1);
+      mbar_init(x_empty(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(a_full(s), kDeqWarps);
+      mbar_init(a_empty(s), 1);
     }
     mbar_init(acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols));
+                 "r"(C::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  PS_TC_TRACE(0, threadIdx.x == 0);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  PS_TC_TRACE(1, threadIdx.x == 0);
 
   if (warp == 0) {
-    // ---------------------------------------------------- TMA producer --
-    // The whole warp walks the loop (keeps it converged); lane 0 issues.
-    constexpr uint32_t kTx = S::kX + (kInt8 ? S::kW8 : S::kA);
+    // ------------------------------------------------- weight producer --
     for (int i = 0; i < nkt; ++i) {
-      const int s = i % STAGES;
-      if (i >= STAGES) {
-        const bool ok = mbar_wait(mma_done(s), ((i / STAGES) - 1) & 1, abort_flag, p.status);
-        if (!__all_sync(0xffffffffu, ok)) break;
-      }
+      const int s = i % RW;
+      if (i >= RW && !warp_wait(w_empty(s), ((i / RW) - 1) & 1, abort_flag, p.status)) break;
+      PS_TC_TRACE(16 + (i & 255) * 8 + 0, lane == 0);
       if (lane == 0) {
-        mbar_expect_tx(tma_full(s), kTx);
-        const int kx = (kt0 + i) * kBK;
-        tma_load_2d(kInt8 ? w8_addr(s) : a_addr(s), &wmap, tma_full(s), kx, n0);
-        tma_load_2d(x_addr(s), &xmap, tma_full(s), kx, m0);
+        if (kInt8 && p.wt) {
+          // NSUB contiguous 8 KB blocks; blocks past the last row block are
+          // not loaded (their rows only feed outputs the epilogue masks).
+          const int b0 = blockIdx.x * NSUB;
+          const int nb = min(NSUB, p.n_blocks - b0);
+          mbar_expect_tx(w_full(s), nb * 8192);
+          for (int sub = 0; sub < nb; ++sub)
+            bulk_load(w_addr(s) + sub * 8192,
+                      p.wt + (static_cast<long long>(b0 + sub) * p.k_tiles + (kt0 + i)) * 8192, 8192, w_full(s));
+        } else {
+          mbar_expect_tx(w_full(s), C::kW);
+          tma_load_2d(w_addr(s), &wmap, w_full(s), (kt0 + i) * kBK, n0);
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 2) {
+    // --------------------------------------------- activation producer --
+    for (int i = 0; i < nkt; ++i) {
+      const int s = i % RX;
+      if (i >= RX && !warp_wait(x_empty(s), ((i / RX) - 1) & 1, abort_flag, p.status)) break;
+      PS_TC_TRACE(16 + (i & 255) * 8 + 1, lane == 0);
+      if (lane == 0) {
+        mbar_expect_tx(x_full(s), C::kX);
+        tma_load_2d(x_addr(s), &xmap, x_full(s), (kt0 + i) * kBK, m0);
       }
       __syncwarp();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer --
-    constexpr uint32_t idesc = instr_desc(!std::is_same<T, __half>::value, kBN, BM);
+    constexpr uint32_t idesc = instr_desc(!std::is_same<T, __half>::value, 128, BM);
     bool ok = nkt > 0;
     for (int i = 0; i < nkt; ++i) {
-      const int s = i % STAGES;
-      ok = __all_sync(0xffffffffu, mbar_wait(kInt8 ? deq_full(s) : tma_full(s), (i / STAGES) & 1, abort_flag,
-                                             p.status));
+      const int sx = i % RX;
+      const int sa = kInt8 ? (i & 1) : (i % RW);
+      ok = warp_wait(kInt8 ? a_full(sa) : w_full(sa), kInt8 ? ((i >> 1) & 1) : ((i / RW) & 1), abort_flag,
+                     p.status);
+      if (ok) ok = warp_wait(x_full(sx), (i / RX) & 1, abort_flag, p.status);
       if (!ok) break;
       tc_fence_after();
+      PS_TC_TRACE(16 + (i & 255) * 8 + 4, lane == 0);
       if (lane == 0) {
+        const uint32_t abase = kInt8 ? a_addr(sa) : w_addr(sa);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(a_addr(s) + kk * 32);
-          const uint64_t bd = smem_desc_sw128(x_addr(s) + kk * 32);
-          mma_f16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t bd = smem_desc_sw128(x_addr(sx) + kk * 32);
+#pragma unroll
+          for (int sub = 0; sub < NSUB; ++sub) {
+            const uint64_t ad = smem_desc_sw128(abase + sub * (128 * 128) + kk * 32);
+            mma_f16(tmem + sub * BM, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
         }
-        mma_commit(mma_done(s));
+        mma_commit(kInt8 ? a_empty(sa) : w_empty(sa));
+        mma_commit(x_empty(sx));
       }
       __syncwarp();
     }
     if (ok && lane == 0) mma_commit(acc_full);
     __syncwarp();
   } else {
+    const int t = threadIdx.x - 96;  // 0 .. 32*kDeqWarps-1
     // --------------------------------------- int8 -> bf16 widening warps --
-    const int t = threadIdx.x - 64;  // 0..127
     if (kInt8) {
       for (int i = 0; i < nkt; ++i) {
-        const int s = i % STAGES;
-        if (!__all_sync(0xffffffffu, mbar_wait(tma_full(s), (i / STAGES) & 1, abort_flag, p.status))) break;
-        const unsigned char* w8 = gbase + (w8_addr(s) - base);
-        unsigned char* a = gbase + (a_addr(s) - base);
+        const int sw = i % RW;
+        const int sa = i & 1;
+        if (!warp_wait(w_full(sw), (i / RW) & 1, abort_flag, p.status)) break;
+        PS_TC_TRACE(16 + (i & 255) * 8 + 5, t == 0);
+        if (i >= 2 && !warp_wait(a_empty(sa), ((i >> 1) - 1) & 1, abort_flag, p.status)) break;
+        PS_TC_TRACE(16 + (i & 255) * 8 + 2, t == 0);
+        const unsigned char* w8 = gbase + (w_addr(sw) - base);
+        unsigned char* a = gbase + (a_addr(sa) - base);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int id = t + 128 * j;  // 512 chunks of 16 int8
-          const int r = id >> 2;
+        for (int j = 0; j < 4 * NSUB * 4 / kDeqWarps; ++j) {
+          const int id = t + 32 * kDeqWarps * j;  // NSUB*512 chunks of 16 int8
+          const int r = id >> 2;       // weight row in the slab
           const int c16 = id & 3;
           const uint4 in = *reinterpret_cast<const uint4*>(w8 + r * 64 + c16 * 16);
           uint4 lo, hi;
@@ -313,77 +412,170 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(deq_full(s));
+        if (lane == 0) {
+          mbar_arrive(a_full(sa));
+          mbar_arrive(w_empty(sw));
+        }
+        PS_TC_TRACE(16 + (i & 255) * 8 + 3, t == 0);
       }
     }
     // ------------------------------------------------------------ epilogue --
-    const bool ok = __all_sync(0xffffffffu, nkt > 0 && mbar_wait(acc_full, 0, abort_flag, p.status));
+    const bool ok = nkt > 0 && warp_wait(acc_full, 0, abort_flag, p.status);
     tc_fence_after();
-    const int q = warp & 3;            // TMEM lane quarter this warp may read
-    const int row = q * 32 + lane;     // weight row within the tile
-    const int n = n0 + row;
+    PS_TC_TRACE(2, t == 0);
+    // acc_full implies every k-tile's MMA (and so every widening pass) is
+    // done and no weight load is in flight: the weight ring is free for the
+    // transpose tiles.
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    float* tp = reinterpret_cast<float*>(gbase + C::kOffEpi) + (warp - 3) * (16 * 32);  // [16 m][32 n]
+    const int cbeg = ((warp - 3) / 4) * (BM / 2);  // this warp's half of the token columns
     const T* bias = static_cast<const T*>(p.bias);
     const T* resid = static_cast<const T*>(p.resid);
     T* y = static_cast<T*>(p.y);
-    const float sc = (n < p.N && p.scale) ? p.scale[n] : 1.f;
-    const float bs = (n < p.N && bias) ? to_f32(bias[n]) : 0.f;
+    const bool vec = (p.N % 8) == 0;
+    const int ml = lane >> 1;         // output row this lane stores
+    const int nl = (lane & 1) * 16;   // first of its 16 columns
     if (ok) {
 #pragma unroll 1
-      for (int c = 0; c < BM; c += 16) {
-        float v[16];
-        __syncwarp();
-        tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c, v);
-        if (n < p.N) {
-          if (p.splits == 1) {
+      for (int sub = 0; sub < NSUB; ++sub) {
+        const int nb = n0 + sub * 128 + q * 32;  // first channel of this warp's 32 rows
+#pragma unroll 1
+        for (int c = cbeg; c < cbeg + BM / 2; c += 16) {
+          float v[16];
+          __syncwarp();
+          tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c + j;
-              if (m < p.M) {
-                float o = v[j] * sc + bs;
-                if (resid) o = to_f32(from_f32<T>(o)) + to_f32(resid[static_cast<long long>(m) * p.N + n]);
-                y[static_cast<long long>(m) * p.N + n] = from_f32<T>(o);
+          for (int j = 0; j < 16; ++j) tp[j * 32 + lane] = v[j];
+          __syncwarp();
+          const int m = m0 + c + ml;
+          const int n = nb + nl;
+          if (m < p.M && n < p.N) {
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = tp[ml * 32 + nl + j];
+            if (p.splits > 1) {
+              float* dst = p.part + (static_cast<long long>(split) * p.M + m) * p.N + n;
+              if (vec && n + 16 <= p.N) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                  *reinterpret_cast<float4*>(dst + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+              } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) dst[j] = o[j];
               }
-            }
-          } else {
+            } else {
+              T* dst = y + static_cast<long long>(m) * p.N + n;
+              const T* rs = resid ? resid + static_cast<long long>(m) * p.N + n : nullptr;
+              if (vec && n + 16 <= p.N) {
+                float sc[16], bs[16], rv[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c + j;
-              if (m < p.M) atomicAdd(p.ws + static_cast<long long>(m) * p.N + n, v[j]);
+                for (int j = 0; j < 16; j += 4) {
+                  const float4 s4 =
+                      p.scale ? *reinterpret_cast<const float4*>(p.scale + n + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+                  sc[j] = s4.x;
+                  sc[j + 1] = s4.y;
+                  sc[j + 2] = s4.z;
+                  sc[j + 3] = s4.w;
+                }
+                if (bias) {
+                  unpack8<T>(*reinterpret_cast<const uint4*>(bias + n), bs);
+                  unpack8<T>(*reinterpret_cast<const uint4*>(bias + n + 8), bs + 8);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) bs[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[j] = o[j] * sc[j] + bs[j];
+                if (rs) {
+                  unpack8<T>(*reinterpret_cast<const uint4*>(rs), rv);
+                  unpack8<T>(*reinterpret_cast<const uint4*>(rs + 8), rv + 8);
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) o[j] = to_f32(from_f32<T>(o[j])) + rv[j];
+                }
+                *reinterpret_cast<uint4*>(dst) = pack8<T>(o);
+                *reinterpret_cast<uint4*>(dst + 8) = pack8<T>(o + 8);
+              } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) {
+                  float v2 = o[j] * (p.scale ? p.scale[n + j] : 1.f) + (bias ? to_f32(bias[n + j]) : 0.f);
+                  if (rs) v2 = to_f32(from_f32<T>(v2)) + to_f32(rs[j]);
+                  dst[j] = from_f32<T>(v2);
+                }
+              }
             }
           }
         }
       }
     }
-    if (p.splits > 1) {
-      // last CTA of this tile finishes: apply scale/bias/residual, re-zero.
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0) {
-        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        const int prev = atomicAdd(p.counters + tile, 1);
-        *last_flag = (prev == p.splits - 1) ? 1 : 0;
-        if (*last_flag) p.counters[tile] = 0;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*last_flag && n < p.N) {
-        __threadfence();
-        const int mend = min(p.M, m0 + BM);
-        for (int m = m0; m < mend; ++m) {
-          float* w = p.ws + static_cast<long long>(m) * p.N + n;
-          const float acc = __ldcg(w);
-          *w = 0.f;
-          float o = acc * sc + bs;
-          if (resid) o = to_f32(from_f32<T>(o)) + to_f32(resid[static_cast<long long>(m) * p.N + n]);
-          y[static_cast<long long>(m) * p.N + n] = from_f32<T>(o);
-        }
-      }
-    }
   }
+  PS_TC_TRACE(3, threadIdx.x == 96);
   tc_fence_before();
   __syncthreads();
+  PS_TC_TRACE(4, threadIdx.x == 0);
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+  }
+}
+
+// Split-K finish: y = scale * sum_s part[s] + bias (+ residual), 4 outputs
+// per thread (16-byte partial loads), grid-stride; reads the partials from L2.
+template <typename T>
+__global__ void splitk_reduce_kernel(T* __restrict__ y, const float* __restrict__ part,
+                                     const float* __restrict__ scale, const T* __restrict__ bias,
+                                     const T* __restrict__ resid, int M, int N, int splits) {
+  const int nq = N / 4;
+  const long long total = static_cast<long long>(M) * nq;
+  const long long plane = static_cast<long long>(M) * N;
+  for (long long it = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; it < total;
+       it += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long m = it / nq;
+    const int n = static_cast<int>(it - m * nq) * 4;
+    const float* src = part + m * N + n;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
+    int s = 1;
+    for (; s + 3 < splits; s += 4) {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(src + s * plane));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(src + (s + 1) * plane));
+      const float4 c = __ldcg(reinterpret_cast<const float4*>(src + (s + 2) * plane));
+      const float4 d = __ldcg(reinterpret_cast<const float4*>(src + (s + 3) * plane));
+      acc.x += (a.x + b.x) + (c.x + d.x);
+      acc.y += (a.y + b.y) + (c.y + d.y);
+      acc.z += (a.z + b.z) + (c.z + d.z);
+      acc.w += (a.w + b.w) + (c.w + d.w);
+    }
+    for (; s < splits; ++s) {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(src + s * plane));
+      acc.x += a.x;
+      acc.y += a.y;
+      acc.z += a.z;
+      acc.w += a.w;
+    }
+    float o[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o[j] = o[j] * (scale ? scale[n + j] : 1.f) + (bias ? to_f32(bias[n + j]) : 0.f);
+      if (resid) o[j] = to_f32(from_f32<T>(o[j])) + to_f32(resid[m * N + n + j]);
+    }
+    T* dst = y + m * N + n;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = from_f32<T>(o[j]);
+  }
+}
+
+// Re-tile a row-major int8 weight [N][K] into 8 KB blocks [N/128][K/64][128][64]
+// (zero padded), so one weight tile of the main loop is one contiguous copy.
+__global__ void tile_int8_kernel(int8_t* __restrict__ dst, const int8_t* __restrict__ src, int N, int K, int kt) {
+  const long long total = static_cast<long long>((N + 127) / 128) * kt * 8192 / 16;  // 16-byte units
+  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < total;
+       u += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long blk = u / 512;  // 8192 / 16
+    const int within = static_cast<int>(u % 512);
+    const int r = within >> 2, c16 = within & 3;
+    const int b = static_cast<int>(blk / kt), k_tile = static_cast<int>(blk % kt);
+    const int n = b * 128 + r, k = k_tile * 64 + c16 * 16;
+    alignas(16) int8_t v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = (n < N && k + i < K) ? src[static_cast<long long>(n) * K + k + i] : 0;
+    reinterpret_cast<uint4*>(dst)[u] = *reinterpret_cast<const uint4*>(v);
   }
 }
 
@@ -414,27 +606,58 @@ bool make_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int esi
 }
 
 struct Plan {
-  int bm, m_tiles, n_tiles, k_tiles, splits, per_split;
+  int nsub, bm, m_tiles, n_tiles, k_tiles, splits, per_split;
 };
 
+int snap_bm(int bm) { return bm <= 32 ? 32 : (bm <= 64 ? 64 : (bm <= 128 ? 128 : (bm <= 192 ? 192 : 256))); }
+
+// Tile plan (rules measured on B200 with CUDA-graph timing over the
+// Qwen2.5-3B projection shapes). Token tiles: one tile up to 256 tokens, else
+// equal tiles. Prefill-sized token tiles (>= 128): wide outputs (N >= 8192)
+// take 256-row weight slabs (two M=128 MMAs share each activation tile);
+// long-K narrow outputs take 256-row slabs with K split so the grid is about
+// one wave; short-K narrow outputs take 128-row slabs split in two.
+// Decode-sized token tiles: 128-row slabs, or 256-row slabs when 128-row
+// slabs would need a second, mostly empty wave; K split when the slabs alone
+// leave most SMs idle. PS_LINEAR_TILE="nsub,bm,splits" overrides (tuning).
 Plan plan(int M, int N, int K) {
   Plan pl{};
-  // token tile: one tile up to 256, else equal tiles of a multiple of 16
   const int mt = (M + 255) / 256;
-  int bm = (M + mt - 1) / mt;
-  bm = (bm + 15) / 16 * 16;
-  if (bm < 16) bm = 16;
-  pl.bm = bm <= 32 ? 32 : (bm <= 64 ? 64 : (bm <= 128 ? 128 : (bm <= 192 ? 192 : 256)));
-  pl.m_tiles = (M + pl.bm - 1) / pl.bm;
-  pl.n_tiles = (N + kBN - 1) / kBN;
+  pl.bm = snap_bm((((M + mt - 1) / mt) + 15) / 16 * 16);
   pl.k_tiles = (K + kBK - 1) / kBK;
-  const int tiles = pl.m_tiles * pl.n_tiles;
+  const int m_tiles = (M + pl.bm - 1) / pl.bm;
+  const int nt1 = (N + 127) / 128, nt2 = (N + 255) / 256;
   int splits = 1;
-  if (tiles < 148) {
-    splits = (148 + tiles - 1) / tiles;
-    const int max_split = pl.k_tiles / 4 > 0 ? pl.k_tiles / 4 : 1;  // >= 4 K tiles per CTA
-    if (splits > max_split) splits = max_split;
+  if (pl.bm >= 128) {
+    if (N >= 8192) {
+      pl.nsub = 2;
+    } else if (K >= 8192) {
+      pl.nsub = 2;
+      splits = 148 / (nt2 * m_tiles);
+      if (splits > 8) splits = 8;
+    } else {
+      pl.nsub = 1;
+      splits = 2;
+    }
+  } else {
+    pl.nsub = (nt1 * m_tiles > 148 && nt2 * m_tiles <= 148) ? 2 : 1;
+    const int tiles = m_tiles * (pl.nsub == 2 ? nt2 : nt1);
+    if (tiles < 100) splits = 148 / tiles;
   }
+  if (const char* env = std::getenv("PS_LINEAR_TILE")) {
+    int a = 0, b = 0, c = 0;
+    if (sscanf(env, "%d,%d,%d", &a, &b, &c) >= 2 && (a == 1 || a == 2)) {
+      pl.nsub = a;
+      pl.bm = snap_bm(b);
+      splits = c > 0 ? c : 1;
+    }
+  }
+  pl.m_tiles = (M + pl.bm - 1) / pl.bm;
+  pl.n_tiles = (N + 128 * pl.nsub - 1) / (128 * pl.nsub);
+  const int max_split = pl.k_tiles / 4 > 0 ? pl.k_tiles / 4 : 1;  // >= 4 K tiles per split
+  if (splits > max_split) splits = max_split;
+  if (splits < 1) splits = 1;
+  if (N % 4 != 0) splits = 1;  // the split-K reduction reads 4 outputs at a time
   pl.per_split = (pl.k_tiles + splits - 1) / splits;
   pl.splits = (pl.k_tiles + pl.per_split - 1) / pl.per_split;
   return pl;
@@ -442,41 +665,59 @@ Plan plan(int M, int N, int K) {
 
 size_t ws_bytes(const Plan& pl, int M, int N) {
   if (pl.splits <= 1) return 0;
-  return 256 + static_cast<size_t>(pl.m_tiles) * pl.n_tiles * sizeof(int) + static_cast<size_t>(M) * N * 4 + 256;
+  return static_cast<size_t>(pl.splits) * M * N * 4 + 256;
 }
 
-template <typename T, bool kInt8, int BM>
-int launch_bm(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
-  constexpr int stage = Smem<T, kInt8, BM, 1>::kStage;
-  constexpr int stages = (200 * 1024) / stage > 8 ? 8 : (200 * 1024) / stage;
-  using S = Smem<T, kInt8, BM, stages>;
-  auto kern = linear_tc_kernel<T, kInt8, BM, stages>;
+template <typename T, bool kInt8, int NSUB, int BM>
+int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
+  using C = Cfg<kInt8, NSUB, BM>;
+  auto kern = linear_tc_kernel<T, kInt8, NSUB, BM>;
   static bool attr_set = false;  // one attribute call per instantiation
   if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes) != cudaSuccess) {
-      ps_host::set_error("linear_tc: cannot reserve %d bytes of shared memory", S::kBytes);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes) != cudaSuccess) {
+      ps_host::set_error("linear_tc: cannot reserve %d bytes of shared memory", C::kBytes);
       return PS_ERR_CUDA;
     }
     attr_set = true;
   }
   dim3 grid(pl.n_tiles, pl.m_tiles, pl.splits);
-  kern<<<grid, kThreads, S::kBytes, s>>>(wm, xm, p);
+  kern<<<grid, kThreads, C::kBytes, s>>>(wm, xm, p);
   ps_host::count_launch();
-  return ps_host::check_launch("linear_tc");
+  int rc = ps_host::check_launch("linear_tc");
+  if (rc != PS_OK || pl.splits == 1) return rc;
+  const long long items = static_cast<long long>(p.M) * (p.N / 4);
+  long long blocks = (items + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  splitk_reduce_kernel<T><<<static_cast<int>(blocks), 256, 0, s>>>(
+      static_cast<T*>(p.y), p.part, p.scale, static_cast<const T*>(p.bias), static_cast<const T*>(p.resid), p.M,
+      p.N, pl.splits);
+  ps_host::count_launch();
+  return ps_host::check_launch("linear_tc(split-K reduce)");
+}
+
+template <typename T, bool kInt8, int NSUB>
+int launch_nsub(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
+  switch (pl.bm) {
+    case 32: return launch_cfg<T, kInt8, NSUB, 32>(wm, xm, p, pl, s);
+    case 64: return launch_cfg<T, kInt8, NSUB, 64>(wm, xm, p, pl, s);
+    case 128: return launch_cfg<T, kInt8, NSUB, 128>(wm, xm, p, pl, s);
+    case 192: return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, s);
+    default: return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, s);
+  }
 }
 
 template <typename T, bool kInt8>
 int launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
-  switch (pl.bm) {
-    case 32: return launch_bm<T, kInt8, 32>(wm, xm, p, pl, s);
-    case 64: return launch_bm<T, kInt8, 64>(wm, xm, p, pl, s);
-    case 128: return launch_bm<T, kInt8, 128>(wm, xm, p, pl, s);
-    case 192: return launch_bm<T, kInt8, 192>(wm, xm, p, pl, s);
-    default: return launch_bm<T, kInt8, 256>(wm, xm, p, pl, s);
-  }
+  return pl.nsub == 2 ? launch_nsub<T, kInt8, 2>(wm, xm, p, pl, s) : launch_nsub<T, kInt8, 1>(wm, xm, p, pl, s);
 }
 
 }  // namespace
+
+#ifdef PS_TRACE
+extern "C" PS_API int ps_debug_tc_trace(unsigned long long* host, int n) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_tc_trace, sizeof(unsigned long long) * n));
+}
+#endif
 
 namespace ps_host {
 
@@ -485,16 +726,35 @@ size_t linear_tc_workspace(int M, int N, int K) {
   return ws_bytes(pl, M, N);
 }
 
+size_t tiled_int8_bytes(int N, int K) {
+  return static_cast<size_t>((N + 127) / 128) * ((K + kBK - 1) / kBK) * 8192;
+}
+
+int tile_int8(int8_t* dst, const int8_t* src, int N, int K, cudaStream_t s) {
+  const int kt = (K + kBK - 1) / kBK;
+  const long long units = static_cast<long long>((N + 127) / 128) * kt * 512;
+  long long blocks = (units + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  tile_int8_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(dst, src, N, K, kt);
+  count_launch();
+  return check_launch("tile_int8_weight");
+}
+
 int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
               const void* resid, int M, int N, int K, int dtype, void* workspace, size_t workspace_bytes,
-              cudaStream_t s) {
+              cudaStream_t s, const int8_t* w_tiled) {
   if (dtype != PS_BF16 && dtype != PS_F16) return PS_ERR_UNSUPPORTED;
   const bool int8 = wdtype == PS_I8;
   if (!int8 && wdtype != dtype) return PS_ERR_UNSUPPORTED;
-  // TMA: global row strides must be multiples of 16 bytes
-  if (K % 16 != 0 || !aligned(x, 16) || !aligned(w, 16)) return PS_ERR_UNSUPPORTED;
+  // TMA: global row strides must be multiples of 16 bytes; the epilogue's
+  // vector loads of scale/bias/residual need 16-byte alignment.
+  if (K % 16 != 0 || !aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !aligned(resid, 16) ||
+      !aligned(bias, 16) || !aligned(scale, 16) || !aligned(w_tiled, 16))
+    return PS_ERR_UNSUPPORTED;
   const Plan pl = plan(M, N, K);
   TcParams p{};
+  p.wt = int8 ? w_tiled : nullptr;
+  p.n_blocks = (N + 127) / 128;
   p.y = y;
   p.scale = scale;
   p.bias = bias;
@@ -512,21 +772,23 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
       set_error("linear: split-K workspace of %zu bytes needed, %zu given", need, workspace_bytes);
       return PS_ERR_INVALID;
     }
-    uintptr_t a = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
-    p.counters = reinterpret_cast<int*>(a);
-    p.ws = reinterpret_cast<float*>((a + pl.m_tiles * pl.n_tiles * sizeof(int) + 255) & ~static_cast<uintptr_t>(255));
+    p.part = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) &
+                                      ~static_cast<uintptr_t>(255));
   }
-  const CUtensorMapDataType xdt = dtype == PS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType xdt =
+      dtype == PS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int bn = 128 * pl.nsub;
   CUtensorMap wm, xm;
   bool ok = make_map(&xm, x, xdt, 2, M, K, kBK, pl.bm, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (int8) ok = ok && make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
-  else ok = ok && make_map(&wm, w, xdt, 2, N, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (int8 && w_tiled) wm = xm;  // unused: the weight arrives by contiguous bulk copies
+  else if (int8) ok = ok && make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, kBK, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else ok = ok && make_map(&wm, w, xdt, 2, N, K, kBK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) {
     set_error("linear: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
     return PS_ERR_CUDA;
   }
-  if (dtype == PS_BF16) return int8 ? launch_t<__nv_bfloat16, true>(wm, xm, p, pl, s)
-                                    : launch_t<__nv_bfloat16, false>(wm, xm, p, pl, s);
+  if (dtype == PS_BF16)
+    return int8 ? launch_t<__nv_bfloat16, true>(wm, xm, p, pl, s) : launch_t<__nv_bfloat16, false>(wm, xm, p, pl, s);
   return int8 ? launch_t<__half, true>(wm, xm, p, pl, s) : launch_t<__half, false>(wm, xm, p, pl, s);
 }
 

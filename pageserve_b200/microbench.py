@@ -4,9 +4,11 @@
     python -m pageserve_b200.microbench sweep          # config 3: W8A16 sweep
     python -m pageserve_b200.microbench attn           # config 2: paged decode attention
 
-Timing: CUDA events on the current stream after warm-up; the weight (or KV
-cache) is replicated over enough copies that the rotation exceeds the 126 MB
-L2, so every launch streams from HBM. Prints one JSON object per case.
+Timing: the timed launches are captured once into a CUDA graph and the graph
+is replayed between CUDA events (device time without host launch overhead —
+the way the model step runs); the weight (or KV cache) is replicated over
+enough copies that the rotation exceeds the 126 MB L2, so every launch
+streams from HBM. Prints one JSON object per case.
 """
 
 from __future__ import annotations
@@ -32,22 +34,34 @@ def _peaks():
     return 6650.0, 1590.0
 
 
-def _time(fn, iters, warmup=3):
+def _time(fn, iters, warmup=3, graph=True):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
+    if not graph:
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / iters
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
     s.record()
-    for _ in range(iters):
-        fn()
+    g.replay()
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
 
 
-def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3):
-    from .quantization import LinearWorkspace, linear16, w8a16_linear
+def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3, tiled=True):
+    from .quantization import LinearWorkspace, linear16, tile_int8_weight, w8a16_linear
     dev = torch.device("cuda")
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -57,6 +71,7 @@ def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3):
         ws = [torch.randn(N, K, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(copies)]
     else:
         ws = [torch.randint(-127, 128, (N, K), device=dev, generator=g, dtype=torch.int8) for _ in range(copies)]
+        tws = [tile_int8_weight(w) for w in ws] if tiled else [None] * copies
     scale = torch.empty(N, 1, device=dev).uniform_(1e-3, 1e-2, generator=g)
     x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
     out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
@@ -69,7 +84,7 @@ def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3):
         if bf16_weight:
             linear16(x, w, out=out, workspace=wsp)
         else:
-            w8a16_linear(x, w, scale, out=out, workspace=wsp)
+            w8a16_linear(x, w, scale, out=out, workspace=wsp, q_tiled=tws[(ctr[0] - 1) % copies])
     ms = _time(f, iters, warmup)
     hbm, tf = _peaks()
     flops = 2.0 * M * N * K
@@ -77,7 +92,8 @@ def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3):
     bound = "tensor" if flops / (tf * 1e12) > byts / (hbm * 1e9) else "hbm"
     ach_tf = flops / ms / 1e9
     ach_gb = byts / ms / 1e6
-    return {"case": "linear", "M": M, "N": N, "K": K, "weight": "bf16" if bf16_weight else "int8", "us": ms * 1e3,
+    return {"case": "linear", "M": M, "N": N, "K": K, "weight": "bf16" if bf16_weight else "int8",
+            "layout": "tiled" if (tiled and not bf16_weight) else "row-major", "us": ms * 1e3,
             "tflops": ach_tf, "gbs": ach_gb, "bound": bound,
             "frac": (ach_tf / tf) if bound == "tensor" else (ach_gb / hbm),
             "ideal_us": max(flops / (tf * 1e12), byts / (hbm * 1e9)) * 1e6}
@@ -136,16 +152,18 @@ def main(argv=None):
     ap.add_argument("--N", type=int, default=22016)
     ap.add_argument("--K", type=int, default=2048)
     ap.add_argument("--bf16-weight", action="store_true")
+    ap.add_argument("--row-major", action="store_true", help="int8 weight row-major (2D TMA) instead of pre-tiled")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
     torch.cuda.init()
     if a.what == "linear":
-        print(json.dumps(bench_linear(a.M, a.N, a.K, a.iters, bf16_weight=a.bf16_weight, warmup=a.warmup)))
+        print(json.dumps(bench_linear(a.M, a.N, a.K, a.iters, bf16_weight=a.bf16_weight, warmup=a.warmup,
+                                      tiled=not a.row_major)))
     elif a.what == "sweep":
         for n, k in SWEEP_NK:
             for m in SWEEP_M:
-                print(json.dumps(bench_linear(m, n, k, a.iters, warmup=a.warmup)), flush=True)
+                print(json.dumps(bench_linear(m, n, k, a.iters, warmup=a.warmup, tiled=not a.row_major)), flush=True)
     else:
         print(json.dumps(bench_attn(iters=a.iters, warmup=a.warmup)))
     from . import _lib

@@ -240,6 +240,10 @@ class PagedCausalLM:
                 input_ln=lw.input_ln, post_ln=lw.post_ln,
                 qkv=_cat_weights([lw.q_w, lw.k_w, lw.v_w], dtype), qkv_b=qkv_b, o=lw.o_w,
                 gate_up=_cat_weights([lw.gate_w, lw.up_w], dtype), down=lw.down_w))
+        for fl in self.fused:  # kernel-side tiled int8 copies, built before any graph capture
+            for w in (fl.qkv, fl.o, fl.gate_up, fl.down):
+                if isinstance(w, QuantizedWeight):
+                    w.tiled()
         self.intermediate_size = (self.layers[0].gate_w.shape[0] if self.layers else 0)
         self.vocab_size = self.embed_tokens.shape[0]
         self.cos_cache, self.sin_cache = build_rope_cache(self.max_position_embeddings, self.head_dim, theta,
@@ -264,7 +268,7 @@ class PagedCausalLM:
     # ------------------------------------------------------------- linear --
     def _linear(self, x, w: Weight, bias=None, residual=None):
         if isinstance(w, QuantizedWeight):
-            return w8a16_linear(x, w.q, w.scale, bias, residual, workspace=self.lin_ws)
+            return w8a16_linear(x, w.q, w.scale, bias, residual, workspace=self.lin_ws, q_tiled=w.tiled())
         return linear16(x, w, bias, residual, workspace=self.lin_ws)
 
     # -------------------------------------------------------------- steps --

@@ -69,13 +69,30 @@ class LinearWorkspace:
 _default_ws: dict[torch.device, LinearWorkspace] = {}
 
 
+def tile_int8_weight(q: torch.Tensor) -> torch.Tensor:
+    """Kernel-side copy of an int8 weight [N][K] in contiguous 8 KB blocks
+    [ceil(N/128)][ceil(K/64)][128][64] (zero padded), streamed by the
+    tensor-core linear with one bulk copy per block."""
+    _lib.require_cuda(q)
+    N, K = q.shape
+    lib = _lib.load()
+    out = torch.empty(lib.ps_tiled_int8_weight_bytes(N, K), dtype=torch.int8, device=q.device)
+    _lib.check(lib.ps_tile_int8_weight(out.data_ptr(), q.contiguous().data_ptr(), N, K, _lib.stream_ptr(q.device)),
+               "tile_int8_weight")
+    return out
+
+
 def w8a16_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None = None,
                  residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                 workspace: LinearWorkspace | None = None) -> torch.Tensor:
+                 workspace: LinearWorkspace | None = None, q_tiled: torch.Tensor | None = None) -> torch.Tensor:
     """y = x @ (q * scale).T + bias (+ residual): F.linear(x, QuantizedWeight.get(), bias)
-    of engine/model.py:168-190, fused. x (..., K) bf16/f16/f32 on CUDA."""
+    of engine/model.py:168-190, fused. x (..., K) bf16/f16/f32 on CUDA.
+    With ``q_tiled`` (from :func:`tile_int8_weight`) and a 16-bit x, the
+    tensor-core kernel streams the pre-tiled copy."""
     _lib.require_cuda(x, q, scale, bias, residual)
     N, K = q.shape
+    if q_tiled is not None and x.dtype in (torch.bfloat16, torch.float16):
+        return _w8a16_tiled(x, q_tiled, scale, N, K, bias, residual, out, workspace)
     lead = x.shape[:-1]
     x2 = x.reshape(-1, K).contiguous()
     M = x2.shape[0]
@@ -93,6 +110,27 @@ def w8a16_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: to
     _lib.check(lib.ps_w8a16_linear(out.data_ptr(), x2.data_ptr(), q.data_ptr(), scale.data_ptr(), _lib.ptr(bias),
                                    _lib.ptr(residual), M, N, K, _lib.dtype_code(x.dtype), _lib.ptr(buf), ws_bytes,
                                    _lib.stream_ptr(x.device)), "w8a16_linear")
+    return out
+
+
+def _w8a16_tiled(x, q_tiled, scale, N, K, bias, residual, out, workspace):
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    if residual is not None:
+        residual = residual.reshape(M, N).contiguous()
+    if bias is not None:
+        bias = bias.to(x.dtype).contiguous()
+    lib = _lib.load()
+    ws_bytes = lib.ps_w8a16_linear_tiled_workspace_size(M, N, K)
+    if workspace is None:
+        workspace = _default_ws.setdefault(x.device, LinearWorkspace())
+    buf = workspace.get(ws_bytes, x.device)
+    _lib.check(lib.ps_w8a16_linear_tiled(out.data_ptr(), x2.data_ptr(), q_tiled.data_ptr(), scale.data_ptr(),
+                                         _lib.ptr(bias), _lib.ptr(residual), M, N, K, _lib.dtype_code(x.dtype),
+                                         _lib.ptr(buf), ws_bytes, _lib.stream_ptr(x.device)), "w8a16_linear_tiled")
     return out
 
 
@@ -153,6 +191,15 @@ class QuantizedWeight:
     def shape(self) -> tuple[int, int]:
         return tuple(self.q.shape)
 
+    def tiled(self) -> torch.Tensor:
+        """The kernel-side 8 KB-block copy of ``q`` (built once, cached)."""
+        t = getattr(self, "_tiled", None)
+        if t is None or t.device != self.q.device:
+            t = tile_int8_weight(self.q)
+            self._tiled = t
+        return t
+
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
                out: torch.Tensor | None = None, workspace: LinearWorkspace | None = None) -> torch.Tensor:
-        return w8a16_linear(x, self.q, self.scale, bias, residual, out, workspace)
+        qt = self.tiled() if x.dtype in (torch.bfloat16, torch.float16) else None
+        return w8a16_linear(x, self.q, self.scale, bias, residual, out, workspace, q_tiled=qt)

@@ -329,3 +329,39 @@ def test_embedding_out_of_range_sets_device_status(dev):
                                         _lib.PS_BF16, _lib.stream_ptr()), "embedding")
     assert _lib.device_status(clear=True) == 3
     assert torch.equal(out[0], table[1]) and not out[1].any()
+
+
+def _tile_ref(q):
+    """numpy restatement of the 8 KB-block layout [N/128][K/64][128][64]."""
+    N, K = q.shape
+    nb, kt = -(-N // 128), -(-K // 64)
+    pad = np.zeros((nb * 128, kt * 64), np.int8)
+    pad[:N, :K] = q
+    return pad.reshape(nb, 128, kt, 64).transpose(0, 2, 1, 3).reshape(-1)
+
+
+@pytest.mark.parametrize("NK", [(136, 896), (300, 880), (2560, 2048)])
+def test_tile_int8_weight_layout(dev, NK):
+    from pageserve_b200.quantization import tile_int8_weight
+    rng = np.random.default_rng(NK[0])
+    q = rng.integers(-127, 128, size=NK).astype(np.int8)
+    t = tile_int8_weight(torch.from_numpy(q).to(dev)).cpu().numpy()
+    assert np.array_equal(t, _tile_ref(q))
+
+
+@pytest.mark.parametrize("M", [1, 5, 64, 130, 576])
+@pytest.mark.parametrize("NK", [(2560, 2048), (136, 896), (300, 880), (2048, 11008)])
+def test_w8a16_linear_tiled_matches_oracle(dev, M, NK):
+    from pageserve_b200.quantization import tile_int8_weight, w8a16_linear
+    N, K = NK
+    rng = np.random.default_rng(M * 13 + N)
+    q = rng.integers(-127, 128, size=(N, K)).astype(np.int8)
+    scale = rng.uniform(1e-3, 1e-2, size=(N, 1)).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b = rng.standard_normal(N, dtype=np.float32)
+    r = rng.standard_normal((M, N), dtype=np.float32)
+    qd = torch.from_numpy(q).to(dev)
+    y = w8a16_linear(_bf16(x, dev), qd, torch.from_numpy(scale).to(dev), _bf16(b, dev), _bf16(r, dev),
+                     q_tiled=tile_int8_weight(qd))
+    ref = ops.quantized_linear(ops.round_bf16(x), q, scale, ops.round_bf16(b)) + ops.round_bf16(r)
+    assert rel_err(y.float().cpu().numpy(), ref) < REL_TOL
