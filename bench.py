@@ -16,8 +16,10 @@ so no flush is needed between steps).
 e2e: the same metric through the public step API (StepGraph.run): per step a
 host->device copy of token ids + metadata from pinned memory and a
 device->host read of the 65 greedy next tokens.
---gpus N > 1: N independent replicas, one per GPU (weak scaling); tensor
-parallelism is not wired into this benchmark yet.
+--gpus N > 1: Megatron tensor parallelism over N ranks (one process per GPU,
+NCCL all-reduce after o_proj and down_proj, vocab-parallel lm_head): one
+model serving the same 64 sequences, so the work is fixed (strong scaling).
+--replicas: N independent single-GPU replicas instead (weak scaling).
 --impl reference: the reference algorithm's CPU path (the oracle port of
 engine/model.py, one forward_step per sequence as engine/runner.py:65-79
 does), on a bounded sample of the same workload, all host threads.
@@ -116,7 +118,7 @@ class Clocks:
 
 # ------------------------------------------------------------- workload ----
 
-def build_workload(device, seed=0):
+def build_workload(device, seed=0, tp=None):
     import numpy as np
     import torch
 
@@ -126,7 +128,7 @@ def build_workload(device, seed=0):
     shape = synthetic.QWEN25_3B
     sd = synthetic.TorchStateDict(shape, seed=seed, device=device)
     m = PagedCausalLM.from_state_dict(sd, shape, device=device, dtype=torch.bfloat16, quantize=True,
-                                      max_position=4096)
+                                      max_position=4096, tp=tp)
     del sd
     torch.cuda.empty_cache()
     nblk_dec = CTX // BLOCK
@@ -178,7 +180,7 @@ def kernel_breakdown(m, w, peaks):
     H, I = m.hidden_size, m.intermediate_size
     x_h = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
     x_i = torch.randn(T, I, device=dev, dtype=torch.bfloat16)
-    x_a = torch.randn(T, m.num_heads * m.head_dim, device=dev, dtype=torch.bfloat16)
+    x_a = torch.randn(T, m.heads_local * m.head_dim, device=dev, dtype=torch.bfloat16)
     ws = LinearWorkspace()
     res = {}
 
@@ -215,7 +217,7 @@ def kernel_breakdown(m, w, peaks):
                       "tflops": 2.0 * xl.shape[0] * V * H / ms / 1e9, "flops": 2.0 * xl.shape[0] * V * H}
     # decode attention: 64 sequences at ctx 2048, rotating over layer caches
     meta = m.make_meta([1] * N_DECODE, [CTX - 1] * N_DECODE, w["tables"][:N_DECODE])
-    q = torch.randn(N_DECODE, m.num_heads, m.head_dim, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(N_DECODE, m.heads_local, m.head_dim, device=dev, dtype=torch.bfloat16)
     aws = AttentionWorkspace()
     ctr = [0]
 
@@ -226,8 +228,8 @@ def kernel_breakdown(m, w, peaks):
                         workspace=aws)
     att()
     ms = time_events(att, 2 * L)
-    kv = N_DECODE * CTX * m.num_kv_heads * m.head_dim * 2 * 2
-    byts = kv + 2 * 2 * N_DECODE * m.num_heads * m.head_dim + 4 * N_DECODE * (CTX // BLOCK)
+    kv = N_DECODE * CTX * m.kv_heads_local * m.head_dim * 2 * 2
+    byts = kv + 2 * 2 * N_DECODE * m.heads_local * m.head_dim + 4 * N_DECODE * (CTX // BLOCK)
     res["attn_decode"] = {"ms": ms, "gbs": byts / ms / 1e6, "bytes": byts}
     return res
 
@@ -307,9 +309,11 @@ def run_gpu(args):
 
     from pageserve_b200 import _lib
     from pageserve_b200.model import StepGraph
+    from pageserve_b200.tensor_parallel import TPGroup
 
     peaks = _peaks()
-    m, w = build_workload(device, seed=rank)
+    tp = TPGroup.from_default() if (world > 1 and not args.replicas) else None
+    m, w = build_workload(device, seed=0 if tp else rank, tp=tp)
     max_blocks = max(len(t) for t in w["tables"])
     g = StepGraph(m, w["q_lens"], max_blocks, CTX, w["start_pos"], w["tables"], w["ids"])
     for _ in range(args.warmup):
@@ -350,17 +354,23 @@ def run_gpu(args):
         t = torch.tensor([ms, e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e_ms = t.tolist()
-    value = world * N_DECODE * args.steps / (ms / 1e3)
-    e2e = world * N_DECODE * args.steps / (e_ms / 1e3)
+    jobs = 1 if tp else world  # TP: one model over all ranks; replicas: one model per rank
+    value = jobs * N_DECODE * args.steps / (ms / 1e3)
+    e2e = jobs * N_DECODE * args.steps / (e_ms / 1e3)
     kb = kernel_breakdown(m, w, peaks) if (rank == 0 and not args.no_breakdown) else None
     if world > 1:
         dist.barrier()
     if rank != 0:
-        dist.destroy_process_group() if world > 1 else None
+        del g
+        if world > 1:
+            dist.destroy_process_group()
         return
     if kb is None:
         print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "ms_per_step": ms / args.steps,
                           "note": "profiling run (no breakdown)"}), flush=True)
+        del g
+        if world > 1:
+            dist.destroy_process_group()
         return
     # dominant kernel: the largest per-step time share among the measured classes
     per_step = {k: v["ms"] * (36 if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode") else 1)
@@ -377,12 +387,14 @@ def run_gpu(args):
         roof = {"kernel": dom, "bound": "hbm", "achieved": d["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": d["gbs"] / peaks["hbm_gbs"], "traffic": None, "algorithmic_per_launch": d["bytes"],
                 "peak_source": peaks["source"]}
-    cpu = cpu_baseline_sample() if not args.no_cpu_baseline else None
+    cpu = cpu_baseline_sample() if (not args.no_cpu_baseline and world == 1) else None
     clocks = clk.summary()
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random init, random KV contents)",
-            "config": _config({"parallelism": f"replicas x{world}" if world > 1 else "single GPU"}),
+            "config": _config({"parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
+                               else "single GPU"}),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": g.h2d_bytes, "d2h_bytes_per_step": g.d2h_bytes,
                     "api": "StepGraph.run (host ids/metadata in, host next tokens out)"},
             "gpu_launches": launches, "launches_per_step": g.launches_per_replay,
@@ -392,6 +404,7 @@ def run_gpu(args):
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "clocks": clocks}
     print(json.dumps(line), flush=True)
+    del g
     if world > 1:
         dist.destroy_process_group()
 
@@ -404,6 +417,7 @@ def main():
     ap.add_argument("--impl", default="pageserve_b200", choices=["pageserve_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-breakdown", action="store_true", help="skip the per-kernel timing (for profiling runs)")
+    ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

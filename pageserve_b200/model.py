@@ -162,9 +162,11 @@ class PagedCausalLM:
 
     @classmethod
     def from_state_dict(cls, state_dict: dict, shape, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
-                        quantize: bool = True, max_position: int | None = None) -> "PagedCausalLM":
+                        quantize: bool = True, max_position: int | None = None, tp=None) -> "PagedCausalLM":
         """Build from an HF-named state dict (numpy or torch tensors) and a
-        ``synthetic.Qwen2Shape`` (the seeded random-init checkpoints)."""
+        ``synthetic.Qwen2Shape`` (the seeded random-init checkpoints). With
+        ``tp`` (a ``tensor_parallel.TPGroup``) this rank loads only its
+        Megatron shard (engine/tensor_parallel.py)."""
         cfg = SimpleNamespace(num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
                               hidden_size=shape.hidden, head_dim=shape.head_dim, rms_norm_eps=shape.rms_eps,
                               rope_theta=shape.rope_theta, rope_parameters=None,
@@ -172,10 +174,10 @@ class PagedCausalLM:
                               num_hidden_layers=shape.num_layers, vocab_size=shape.vocab,
                               intermediate_size=shape.intermediate, tie_word_embeddings=shape.tie_embeddings)
         obj = cls.__new__(cls)
-        obj._init(cfg, state_dict, device, dtype, quantize, shape.rope_theta)
+        obj._init(cfg, state_dict, device, dtype, quantize, shape.rope_theta, tp)
         return obj
 
-    def _init(self, config, sd, device, dtype, quantize, theta):
+    def _init(self, config, sd, device, dtype, quantize, theta, tp=None):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback)")
@@ -190,9 +192,21 @@ class PagedCausalLM:
         self.num_kv_heads = config.num_key_value_heads
         self.hidden_size = config.hidden_size
         self.head_dim = getattr(config, "head_dim", None) or self.hidden_size // self.num_heads
+        self.tp = tp if (tp is not None and tp.world > 1) else None
+        self.shard = None
+        if self.tp is not None:
+            from .tensor_parallel import ShardPlan
+            inter = config.intermediate_size if hasattr(config, "intermediate_size") else \
+                int(sd["model.layers.0.mlp.gate_proj.weight"].shape[0])
+            vocab = int(sd["model.embed_tokens.weight"].shape[0])
+            self.shard = ShardPlan(self.tp.rank, self.tp.world, self.num_heads, self.num_kv_heads, self.head_dim,
+                                   inter, vocab)
         self.rms_eps = config.rms_norm_eps
         self.rope_theta = theta
         self.max_position_embeddings = config.max_position_embeddings
+
+        self.heads_local = self.shard.heads_local if self.shard else self.num_heads
+        self.kv_heads_local = self.shard.kv_heads_local if self.shard else self.num_kv_heads
 
         def T(key):
             v = sd[key]
@@ -201,17 +215,63 @@ class PagedCausalLM:
         def dev(key, dt=None):
             return T(key).to(device=self.device, dtype=dt or dtype).contiguous()
 
+        sp = self.shard
+
+        def rows_of(key):
+            """Column-parallel rows of this rank (None = all)."""
+            if sp is None:
+                return None
+            if key.endswith(("q_proj.weight", "q_proj.bias")):
+                return sp.q_rows()
+            if key.endswith(("k_proj.weight", "v_proj.weight", "k_proj.bias", "v_proj.bias")):
+                return sp.kv_rows()
+            if key.endswith(("gate_proj.weight", "up_proj.weight")):
+                return list(sp.inter_cols)
+            return None
+
+        def cols_of(key):
+            """Row-parallel input columns of this rank (None = all)."""
+            if sp is None:
+                return None
+            if key.endswith("o_proj.weight"):
+                return sp.q_rows()
+            if key.endswith("down_proj.weight"):
+                return list(sp.inter_cols)
+            return None
+
         def load_weight(key) -> Weight:
             w = T(key).to(self.device)
+            rows, cols = rows_of(key), cols_of(key)
+            if rows is not None:  # row slices quantize identically (per-row scales)
+                w = w[torch.as_tensor(rows, device=w.device)]
             if quantize:
                 qw = QuantizedWeight(w)
                 qw.dtype = dtype
+                if cols is not None:  # keep the full-row scale: partials sum to the unsharded linear
+                    qw.q = qw.q[:, torch.as_tensor(cols, device=w.device)].contiguous()
                 return qw
+            if cols is not None:
+                w = w[:, torch.as_tensor(cols, device=w.device)]
             return w.to(dtype).contiguous()
+
+        def bias(key):
+            if key not in sd:
+                return None
+            b = T(key).to(self.device)
+            rows = rows_of(key)
+            if rows is not None:
+                b = b[torch.as_tensor(rows, device=b.device)]
+            return b.to(dtype).contiguous()
 
         self.embed_tokens = dev("model.embed_tokens.weight")
         self.final_norm_w = dev("model.norm.weight")
-        self.lm_head_w = dev("lm_head.weight") if "lm_head.weight" in sd else self.embed_tokens
+        lm = dev("lm_head.weight") if "lm_head.weight" in sd else self.embed_tokens
+        self.vocab_offset = 0
+        if sp is not None:
+            vr = sp.vocab_rows
+            lm = lm[vr.start:vr.stop].contiguous()
+            self.vocab_offset = vr.start
+        self.lm_head_w = lm
         self.layers: list[LayerWeights] = []
         self.fused: list[FusedLayer] = []
         for i in range(config.num_hidden_layers):
@@ -226,12 +286,12 @@ class PagedCausalLM:
                 gate_w=load_weight(p + "mlp.gate_proj.weight"),
                 up_w=load_weight(p + "mlp.up_proj.weight"),
                 down_w=load_weight(p + "mlp.down_proj.weight"),
-                q_b=dev(p + "self_attn.q_proj.bias") if p + "self_attn.q_proj.bias" in sd else None,
-                k_b=dev(p + "self_attn.k_proj.bias") if p + "self_attn.k_proj.bias" in sd else None,
-                v_b=dev(p + "self_attn.v_proj.bias") if p + "self_attn.v_proj.bias" in sd else None,
+                q_b=bias(p + "self_attn.q_proj.bias"),
+                k_b=bias(p + "self_attn.k_proj.bias"),
+                v_b=bias(p + "self_attn.v_proj.bias"),
             )
             self.layers.append(lw)
-            hq, hkv, d = self.num_heads, self.num_kv_heads, self.head_dim
+            hq, hkv, d = self.heads_local, self.kv_heads_local, self.head_dim
             zb = lambda n: torch.zeros(n, dtype=dtype, device=self.device)  # noqa: E731
             qkv_b = torch.cat([lw.q_b if lw.q_b is not None else zb(hq * d),
                                lw.k_b if lw.k_b is not None else zb(hkv * d),
@@ -244,7 +304,7 @@ class PagedCausalLM:
             for w in (fl.qkv, fl.o, fl.gate_up, fl.down):
                 if isinstance(w, QuantizedWeight):
                     w.tiled()
-        self.intermediate_size = (self.layers[0].gate_w.shape[0] if self.layers else 0)
+        self.intermediate_size = (self.layers[0].gate_w.shape[0] if self.layers else 0)  # local under TP
         self.vocab_size = self.embed_tokens.shape[0]
         self.cos_cache, self.sin_cache = build_rope_cache(self.max_position_embeddings, self.head_dim, theta,
                                                           self.device, dtype)
@@ -259,7 +319,7 @@ class PagedCausalLM:
     # ------------------------------------------------------------ memory --
     def allocate_kv_cache(self, num_blocks: int, block_size: int) -> None:
         """engine/model.py:143-147: (L, NB, bs, Hkv, D) zeros."""
-        shape = (len(self.layers), num_blocks, block_size, self.num_kv_heads, self.head_dim)
+        shape = (len(self.layers), num_blocks, block_size, self.kv_heads_local, self.head_dim)
         self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
         self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
         self.block_size = block_size
@@ -284,7 +344,8 @@ class PagedCausalLM:
 
     def _forward(self, ids: torch.Tensor, meta: StepMeta, logits_rows: torch.Tensor | None):
         T = ids.shape[0]
-        H, hq, hkv, d = self.hidden_size, self.num_heads, self.num_kv_heads, self.head_dim
+        H, hq, hkv, d = self.hidden_size, self.heads_local, self.kv_heads_local, self.head_dim
+        lead = self.tp is None or self.tp.rank == 0  # adds the residual exactly once
         lib = _lib.load()
         stream = _lib.stream_ptr(self.device)
         x = torch.empty((T, H), dtype=self.dtype, device=self.device)
@@ -312,13 +373,17 @@ class PagedCausalLM:
             for (s, e, _) in runs:
                 paged_attention(q, kc, vc, meta.block_tables[s:e], meta.cu_q[s:e + 1], meta.start_pos[s:e],
                                 max(meta.q_lens[s:e]), max(meta.ctx_lens[s:e]), out=attn, workspace=self.attn_ws)
-            x = self._linear(attn.view(T, hq * d), fl.o, residual=x)
+            x = self._linear(attn.view(T, hq * d), fl.o, residual=x if lead else None)
+            if self.tp is not None:
+                self.tp.all_reduce_(x)
             h = rms_norm_fused(x, fl.post_ln, self.rms_eps)
             gu = self._linear(h, fl.gate_up)
             act = torch.empty((T, self.intermediate_size), dtype=self.dtype, device=self.device)
             _lib.check(lib.ps_silu_mul(act.data_ptr(), gu.data_ptr(), T, self.intermediate_size,
                                        _lib.dtype_code(self.dtype), stream), "silu_mul")
-            x = self._linear(act, fl.down, residual=x)
+            x = self._linear(act, fl.down, residual=x if lead else None)
+            if self.tp is not None:
+                self.tp.all_reduce_(x)
         if logits_rows is not None:
             x = x.index_select(0, logits_rows)
         x = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
@@ -332,7 +397,7 @@ class PagedCausalLM:
         ids = input_ids.to(device=self.device, dtype=torch.int64).reshape(-1)
         T = ids.shape[0]
         meta = self.make_meta([T], [int(start_pos)], [list(block_table)])
-        return self._forward(ids, meta, None)
+        return self.gather_logits(self._forward(ids, meta, None))
 
     def forward_batch(self, input_ids, q_lens: list[int], start_pos: list[int], block_tables: list[list[int]],
                       return_logits: bool = True):
@@ -347,8 +412,26 @@ class PagedCausalLM:
         meta = self.make_meta(q_lens, start_pos, block_tables)
         last = meta.cu_q[1:].to(torch.int64) - 1
         logits = self._forward(ids, meta, last)
-        nxt = self.argmax(logits)
-        return (logits if return_logits else None), nxt
+        nxt = self.next_tokens(logits)
+        return (self.gather_logits(logits) if return_logits else None), nxt
+
+    def gather_logits(self, logits: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary logits (all-gathered over the vocab shards under TP)."""
+        if self.tp is None:
+            return logits
+        import torch.distributed as dist
+        parts = [torch.empty_like(logits) for _ in range(self.tp.world)]
+        dist.all_gather(parts, logits.contiguous(), group=self.tp.group)
+        return torch.cat(parts, dim=-1)[:, :self.vocab_size]
+
+    def next_tokens(self, logits: torch.Tensor) -> torch.Tensor:
+        """Greedy next token per row (int32); distributed over vocab shards under TP."""
+        idx = self.argmax(logits)
+        if self.tp is None:
+            return idx
+        from .tensor_parallel import distributed_argmax
+        vals = logits.gather(1, idx.to(torch.int64).unsqueeze(1)).squeeze(1).float()
+        return distributed_argmax(vals, idx, self.vocab_offset, self.tp).to(torch.int32)
 
     def argmax(self, logits: torch.Tensor) -> torch.Tensor:
         """int(logits[row].argmax()) for every row, on the device."""
@@ -410,7 +493,7 @@ class StepGraph:
     def _body(self):
         last = self.meta_dev[1:self.B + 1].to(torch.int64) - 1
         logits = self.m._forward(self.ids_dev, self.meta, last)
-        return logits, self.m.argmax(logits)
+        return logits, self.m.next_tokens(logits)
 
     def replay(self) -> None:
         """Re-run the captured step on the current device buffers."""

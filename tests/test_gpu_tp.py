@@ -1,0 +1,60 @@
+"""Tensor parallelism on 2 GPUs (NCCL): a TP=2 sharded model produces the
+TP=1 model's logits and greedy tokens. Skipped with fewer than 2 GPUs."""
+
+import os
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _tp_worker(rank, world, port, out_file):
+    import datetime
+
+    import torch.distributed as dist
+
+    from pageserve_b200 import synthetic
+    from pageserve_b200.model import PagedCausalLM
+    from pageserve_b200.tensor_parallel import TPGroup
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    shape = synthetic.TINY
+    sd = synthetic.generate_state_dict(shape, seed=9, perturb_norms_biases=True)
+    m = PagedCausalLM.from_state_dict(sd, shape, device=f"cuda:{rank}", quantize=True, tp=TPGroup(rank, world))
+    m.allocate_kv_cache(40, 4)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, shape.vocab, size=n) for n in (11, 23)]
+    tables = [list(range(0, 6)), list(range(6, 14))]
+    lg0 = m.forward_step(torch.from_numpy(prompts[0]), tables[0], 0)
+    lg1, tok = m.forward_batch(np.concatenate([prompts[1][:20], [7]]), [20, 1], [0, 11], [tables[1], tables[0]])
+    res = {"lg0": lg0.float().cpu(), "lg1": lg1.float().cpu(), "tok": tok.cpu()}
+    if rank == 0:
+        ref = PagedCausalLM.from_state_dict(sd, shape, device="cuda:0", quantize=True)
+        ref.allocate_kv_cache(40, 4)
+        r0 = ref.forward_step(torch.from_numpy(prompts[0]), tables[0], 0)
+        r1, rt = ref.forward_batch(np.concatenate([prompts[1][:20], [7]]), [20, 1], [0, 11], [tables[1], tables[0]])
+        res.update(ref0=r0.float().cpu(), ref1=r1.float().cpu(), reftok=rt.cpu())
+    torch.save(res, f"{out_file}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_tp2_matches_tp1():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_tp_worker, args=(2, 29517, os.path.join(tmp, "r")), nprocs=2, join=True)
+        a = torch.load(os.path.join(tmp, "r.0"), weights_only=True)
+        b = torch.load(os.path.join(tmp, "r.1"), weights_only=True)
+    for k in ("lg0", "lg1", "tok"):
+        assert torch.equal(a[k], b[k]), f"ranks disagree on {k}"
+    for got, ref in ((a["lg0"], a["ref0"]), (a["lg1"], a["ref1"])):
+        err = float((got - ref).abs().max() / ref.abs().max())
+        assert err < 2e-2, err
+    assert a["tok"].tolist() == a["reftok"].tolist()
