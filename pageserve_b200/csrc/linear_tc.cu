@@ -18,15 +18,21 @@
 //               NSUB x 4 per k-tile, and commits to the rings' empty barriers
 //   warp 2      activation producer: TMA of the bf16 tile (BM x 128 B,
 //               128B swizzle) into its ring
-//   warps 3..10 widen int8 -> bf16 (exact: |q| <= 127) into a 2-deep ring in
-//               the 128B-swizzled K-major UMMA layout, running up to two
-//               k-tiles ahead of the MMA (two warps per SM sub-partition: the
-//               widening is latency bound); then the epilogue from TMEM
-//               (tcgen05.ld 32x32b; warp w reads lane quarter w%4, half of
-//               the columns), transposed through shared memory so each lane
-//               stores 16 consecutive outputs (scale, bias, residual)
+//   warps 3..10 widen int8 -> bf16 (exact: |q| <= 127) straight into a
+//               2-deep ring of MMA A operands in tensor memory (tcgen05.st; one
+//               weight row per lane, K packed two bf16 per column), running up
+//               to two k-tiles ahead of the MMA, which reads A from TMEM
+//               (tcgen05.mma ... [a_tmem]) and only the activations from
+//               shared memory; then the epilogue from TMEM (tcgen05.ld 32x32b;
+//               warp w reads lane quarter w%4, half of the columns),
+//               transposed through shared memory so each lane stores 16
+//               consecutive outputs (scale, bias, residual)
 // The weight stream runs ahead independently of the MMA, so HBM latency is
 // hidden by the weight ring depth rather than by the MMA's commit chain.
+// Keeping the widened weights in TMEM takes their write and the MMA's read
+// (64 KB per k-tile at 256 rows) off shared memory, whose bandwidth bounds
+// this loop. bf16/f16 weights (the lm_head) skip the widening: TMA lands
+// them in shared memory as the MMA's A operand directly.
 // Small-N shapes split K across CTAs: each split stores float32 partials
 // (no atomics) and a separate wide kernel reduces them and applies the
 // epilogue (a single CTA reducing a whole tile was latency bound).
@@ -170,6 +176,39 @@ PS_DEVICE void tmem_ld16(uint32_t addr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+PS_DEVICE void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+PS_DEVICE void tmem_st16(uint32_t addr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+PS_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+PS_DEVICE void tmem_ld32(uint32_t addr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 16 signed bytes -> 16 bf16 (exact). For byte b = s*128 + u (two's
 // complement, u = low 7 bits): value = (128 + u) - (128 + 128*s); both
 // terms are exact bf16 built by byte permutes, one packed subtract per pair.
@@ -232,9 +271,11 @@ struct Cfg {
   static constexpr int kBN = 128 * NSUB;
   static constexpr int kW = kInt8 ? kBN * kBK : kBN * kBK * 2;  // weight ring stage
   static constexpr int kX = BM * kBK * 2;                        // activation ring stage
-  static constexpr int kA = kInt8 ? kBN * kBK * 2 : 0;           // widened operand stage
-  static constexpr int kAS = kInt8 ? 2 : 0;                      // widened operand stages
-  static constexpr int kEpi = kDeqWarps * 16 * 32 * 4;           // per-warp transpose tiles
+  static constexpr int kA = 0;                                   // widened operands live in TMEM
+  static constexpr int kAS = 0;
+  static constexpr int kAccCols = NSUB * BM;                       // fp32 accumulators
+  static constexpr int kACols = kInt8 ? NSUB * (kBK / 2) : 0;      // one TMEM A stage (2 bf16 per column)
+  static constexpr int kEpi = kDeqWarps * 32 * 33 * 4;           // per-warp padded 32x32 transpose tiles
   static constexpr int kRX0 = (96 * 1024) / kX;
   static constexpr int kRX = kRX0 < 2 ? 2 : (kRX0 > 8 ? 8 : kRX0);
   static constexpr int kRW0 = (kSmemBudget - kAS * kA - kRX * kX) / kW;
@@ -247,11 +288,12 @@ struct Cfg {
   static constexpr int kOffEpi = kOffW;
   static constexpr int kOffBar = kOffX + kRX * kX;
   static constexpr int kBytes = kOffBar + 512 + 1024;
-  static constexpr int kTmemCols = NSUB * BM <= 32 ? 32 : (NSUB * BM <= 64 ? 64 : (NSUB * BM <= 128 ? 128 :
-                                   (NSUB * BM <= 256 ? 256 : 512)));
+  static constexpr int kTmemNeed = kAccCols + 2 * kACols;  // accumulators + two A stages
+  static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 :
+                                   (kTmemNeed <= 256 ? 256 : 512)));
   static_assert(kBytes <= 227 * 1024, "shared memory plan too large");
   static_assert(kRW * kW >= kEpi, "epilogue tiles alias the weight ring");
-  static_assert(NSUB * BM <= 512, "TMEM columns");
+  static_assert(kTmemNeed <= 512, "TMEM columns");
   static_assert(kW % 1024 == 0 && kX % 1024 == 0 && kA % 1024 == 0, "1024-byte aligned stages");
 };
 
@@ -367,14 +409,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       PS_TC_TRACE(16 + (i & 255) * 8 + 4, lane == 0);
       if (lane == 0) {
-        const uint32_t abase = kInt8 ? a_addr(sa) : w_addr(sa);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           const uint64_t bd = smem_desc_sw128(x_addr(sx) + kk * 32);
 #pragma unroll
           for (int sub = 0; sub < NSUB; ++sub) {
-            const uint64_t ad = smem_desc_sw128(abase + sub * (128 * 128) + kk * 32);
-            mma_f16(tmem + sub * BM, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kInt8) {
+              const uint32_t ta = tmem + C::kAccCols + sa * C::kACols + sub * (kBK / 2) + kk * 8;
+              mma_ts(tmem + sub * BM, ta, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint64_t ad = smem_desc_sw128(w_addr(sa) + sub * (128 * 128) + kk * 32);
+              mma_f16(tmem + sub * BM, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
         }
         mma_commit(kInt8 ? a_empty(sa) : w_empty(sa));
@@ -386,31 +432,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     const int t = threadIdx.x - 96;  // 0 .. 32*kDeqWarps-1
-    // --------------------------------------- int8 -> bf16 widening warps --
+    // ------------------------------------- int8 -> bf16 widening into TMEM --
+    // Warp (q = warp % 4, h = (warp - 3) / 4) owns TMEM lanes [32q, 32q+32):
+    // NSUB = 2: sub-tile h, the row's whole K tile (64 values, 32 columns);
+    // NSUB = 1: the row's K half h (32 values, 16 columns). Each lane reads
+    // its weight row from the (pre-swizzled) int8 stage and widens it.
     if (kInt8) {
+      const int q = warp & 3;
+      const int h = (warp - 3) >> 2;
+      const int rin = q * 32 + lane;                        // row inside the 128-row block
+      const int sub = NSUB == 2 ? h : 0;
+      const int swz = p.wt ? ((rin >> 1) & 3) : 0;           // chunk slot swizzle of the tiled layout
+      constexpr int kChunks = NSUB == 2 ? 4 : 2;             // 16-byte chunks this lane widens
+      const int c0 = NSUB == 2 ? 0 : 2 * h;
+      const uint32_t tcol0 = (NSUB == 2 ? sub * (kBK / 2) : h * (kBK / 4));
       for (int i = 0; i < nkt; ++i) {
         const int sw = i % RW;
         const int sa = i & 1;
         if (!warp_wait(w_full(sw), (i / RW) & 1, abort_flag, p.status)) break;
         PS_TC_TRACE(16 + (i & 255) * 8 + 5, t == 0);
         if (i >= 2 && !warp_wait(a_empty(sa), ((i >> 1) - 1) & 1, abort_flag, p.status)) break;
+        tc_fence_after();
         PS_TC_TRACE(16 + (i & 255) * 8 + 2, t == 0);
-        const unsigned char* w8 = gbase + (w_addr(sw) - base);
-        unsigned char* a = gbase + (a_addr(sa) - base);
+        const unsigned char* row = gbase + (w_addr(sw) - base) + sub * 8192 + rin * 64;
+        uint32_t words[kChunks * 8];
 #pragma unroll
-        for (int j = 0; j < 4 * NSUB * 4 / kDeqWarps; ++j) {
-          const int id = t + 32 * kDeqWarps * j;  // NSUB*512 chunks of 16 int8
-          const int r = id >> 2;       // weight row in the slab
-          const int c16 = id & 3;
-          const uint4 in = *reinterpret_cast<const uint4*>(w8 + r * 64 + c16 * 16);
+        for (int c = 0; c < kChunks; ++c) {
+          const uint4 in = *reinterpret_cast<const uint4*>(row + (((c0 + c) ^ swz) << 4));
           uint4 lo, hi;
           if constexpr (std::is_same<T, __half>::value) widen16_f16(in, lo, hi);
           else widen16_bf16(in, lo, hi);
-          const int c0 = (2 * c16) ^ (r & 7), c1 = (2 * c16 + 1) ^ (r & 7);
-          *reinterpret_cast<uint4*>(a + r * 128 + c0 * 16) = lo;
-          *reinterpret_cast<uint4*>(a + r * 128 + c1 * 16) = hi;
+          words[c * 8 + 0] = lo.x; words[c * 8 + 1] = lo.y; words[c * 8 + 2] = lo.z; words[c * 8 + 3] = lo.w;
+          words[c * 8 + 4] = hi.x; words[c * 8 + 5] = hi.y; words[c * 8 + 6] = hi.z; words[c * 8 + 7] = hi.w;
         }
-        fence_proxy_async();
+        const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::kAccCols + sa * C::kACols + tcol0;
+        tmem_st16(ta, words);
+        if constexpr (kChunks == 4) tmem_st16(ta + 16, words + 16);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(a_full(sa));
@@ -420,82 +479,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     // ------------------------------------------------------------ epilogue --
+    // Lane = weight row n (its TMEM lane): scale and bias are per-lane
+    // scalars applied in that layout; 32 token columns at a time go through a
+    // padded shared-memory transpose so each lane then owns one token row and
+    // stores 32 consecutive outputs (64 bytes) with 16-byte stores.
     const bool ok = nkt > 0 && warp_wait(acc_full, 0, abort_flag, p.status);
     tc_fence_after();
     PS_TC_TRACE(2, t == 0);
     // acc_full implies every k-tile's MMA (and so every widening pass) is
     // done and no weight load is in flight: the weight ring is free for the
     // transpose tiles.
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
-    float* tp = reinterpret_cast<float*>(gbase + C::kOffEpi) + (warp - 3) * (16 * 32);  // [16 m][32 n]
-    const int cbeg = ((warp - 3) / 4) * (BM / 2);  // this warp's half of the token columns
+    const int q = warp & 3;             // TMEM lane quarter this warp may read
+    const int h = (warp - 3) >> 2;      // which 32-column chunks (alternating)
+    float* tp = reinterpret_cast<float*>(gbase + C::kOffEpi) + (warp - 3) * (32 * 33);
     const T* bias = static_cast<const T*>(p.bias);
     const T* resid = static_cast<const T*>(p.resid);
     T* y = static_cast<T*>(p.y);
-    const bool vec = (p.N % 8) == 0;
-    const int ml = lane >> 1;         // output row this lane stores
-    const int nl = (lane & 1) * 16;   // first of its 16 columns
+    const bool part = p.splits > 1;
     if (ok) {
 #pragma unroll 1
       for (int sub = 0; sub < NSUB; ++sub) {
-        const int nb = n0 + sub * 128 + q * 32;  // first channel of this warp's 32 rows
+        const int nb = n0 + sub * 128 + q * 32;  // first weight row of this warp's 32
+        const int n = nb + lane;                 // this lane's row (before the transpose)
+        const float sc = (!part && n < p.N && p.scale) ? p.scale[n] : 1.f;
+        const float bs = (!part && n < p.N && bias) ? to_f32(bias[n]) : 0.f;
 #pragma unroll 1
-        for (int c = cbeg; c < cbeg + BM / 2; c += 16) {
-          float v[16];
+        for (int c = 32 * h; c < BM; c += 64) {
+          float v[32];
           __syncwarp();
-          tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
+          tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) tp[j * 32 + lane] = v[j];
+          for (int j = 0; j < 32; ++j) tp[j * 33 + lane] = v[j] * sc + bs;  // [token j][row lane]
           __syncwarp();
-          const int m = m0 + c + ml;
-          const int n = nb + nl;
-          if (m < p.M && n < p.N) {
-            float o[16];
+          const int m = m0 + c + lane;  // this lane's token row after the transpose
+          if (m < p.M && nb < p.N) {
+            float o[32];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] = tp[ml * 32 + nl + j];
-            if (p.splits > 1) {
-              float* dst = p.part + (static_cast<long long>(split) * p.M + m) * p.N + n;
-              if (vec && n + 16 <= p.N) {
+            for (int j = 0; j < 32; ++j) o[j] = tp[lane * 33 + j];
+            const int cnt = min(32, p.N - nb);
+            if (part) {
+              float* dst = p.part + (static_cast<long long>(split) * p.M + m) * p.N + nb;
+              if (cnt == 32 && (p.N % 4) == 0) {
 #pragma unroll
-                for (int j = 0; j < 16; j += 4)
+                for (int j = 0; j < 32; j += 4)
                   *reinterpret_cast<float4*>(dst + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
               } else {
-                for (int j = 0; j < 16 && n + j < p.N; ++j) dst[j] = o[j];
+                for (int j = 0; j < cnt; ++j) dst[j] = o[j];
               }
             } else {
-              T* dst = y + static_cast<long long>(m) * p.N + n;
-              const T* rs = resid ? resid + static_cast<long long>(m) * p.N + n : nullptr;
-              if (vec && n + 16 <= p.N) {
-                float sc[16], bs[16], rv[16];
-#pragma unroll
-                for (int j = 0; j < 16; j += 4) {
-                  const float4 s4 =
-                      p.scale ? *reinterpret_cast<const float4*>(p.scale + n + j) : make_float4(1.f, 1.f, 1.f, 1.f);
-                  sc[j] = s4.x;
-                  sc[j + 1] = s4.y;
-                  sc[j + 2] = s4.z;
-                  sc[j + 3] = s4.w;
-                }
-                if (bias) {
-                  unpack8<T>(*reinterpret_cast<const uint4*>(bias + n), bs);
-                  unpack8<T>(*reinterpret_cast<const uint4*>(bias + n + 8), bs + 8);
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) bs[j] = 0.f;
-                }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) o[j] = o[j] * sc[j] + bs[j];
+              T* dst = y + static_cast<long long>(m) * p.N + nb;
+              const T* rs = resid ? resid + static_cast<long long>(m) * p.N + nb : nullptr;
+              if (cnt == 32 && (p.N % 8) == 0) {
                 if (rs) {
-                  unpack8<T>(*reinterpret_cast<const uint4*>(rs), rv);
-                  unpack8<T>(*reinterpret_cast<const uint4*>(rs + 8), rv + 8);
+                  float rv[32];
 #pragma unroll
-                  for (int j = 0; j < 16; ++j) o[j] = to_f32(from_f32<T>(o[j])) + rv[j];
+                  for (int j = 0; j < 32; j += 8) unpack8<T>(*reinterpret_cast<const uint4*>(rs + j), rv + j);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) o[j] = to_f32(from_f32<T>(o[j])) + rv[j];
                 }
-                *reinterpret_cast<uint4*>(dst) = pack8<T>(o);
-                *reinterpret_cast<uint4*>(dst + 8) = pack8<T>(o + 8);
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = pack8<T>(o + j);
               } else {
-                for (int j = 0; j < 16 && n + j < p.N; ++j) {
-                  float v2 = o[j] * (p.scale ? p.scale[n + j] : 1.f) + (bias ? to_f32(bias[n + j]) : 0.f);
+                for (int j = 0; j < cnt; ++j) {
+                  float v2 = o[j];
                   if (rs) v2 = to_f32(from_f32<T>(v2)) + to_f32(rs[j]);
                   dst[j] = from_f32<T>(v2);
                 }
@@ -563,6 +609,9 @@ __global__ void splitk_reduce_kernel(T* __restrict__ y, const float* __restrict_
 
 // Re-tile a row-major int8 weight [N][K] into 8 KB blocks [N/128][K/64][128][64]
 // (zero padded), so one weight tile of the main loop is one contiguous copy.
+// Inside a block, the 16-byte chunk c of row r sits in slot c ^ ((r >> 1) & 3),
+// so the widening warps (one row per lane) read shared memory without bank
+// conflicts.
 __global__ void tile_int8_kernel(int8_t* __restrict__ dst, const int8_t* __restrict__ src, int N, int K, int kt) {
   const long long total = static_cast<long long>((N + 127) / 128) * kt * 8192 / 16;  // 16-byte units
   for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < total;
@@ -575,7 +624,8 @@ __global__ void tile_int8_kernel(int8_t* __restrict__ dst, const int8_t* __restr
     alignas(16) int8_t v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = (n < N && k + i < K) ? src[static_cast<long long>(n) * K + k + i] : 0;
-    reinterpret_cast<uint4*>(dst)[u] = *reinterpret_cast<const uint4*>(v);
+    const long long slot = blk * 512 + r * 4 + (c16 ^ ((r >> 1) & 3));
+    reinterpret_cast<uint4*>(dst)[slot] = *reinterpret_cast<const uint4*>(v);
   }
 }
 
@@ -620,7 +670,7 @@ int snap_bm(int bm) { return bm <= 32 ? 32 : (bm <= 64 ? 64 : (bm <= 128 ? 128 :
 // Decode-sized token tiles: 128-row slabs, or 256-row slabs when 128-row
 // slabs would need a second, mostly empty wave; K split when the slabs alone
 // leave most SMs idle. PS_LINEAR_TILE="nsub,bm,splits" overrides (tuning).
-Plan plan(int M, int N, int K) {
+Plan plan(int M, int N, int K, bool int8) {
   Plan pl{};
   const int mt = (M + 255) / 256;
   pl.bm = snap_bm((((M + mt - 1) / mt) + 15) / 16 * 16);
@@ -651,6 +701,11 @@ Plan plan(int M, int N, int K) {
       pl.bm = snap_bm(b);
       splits = c > 0 ? c : 1;
     }
+  }
+  if (int8 && pl.nsub == 2 && pl.bm > 192) {  // TMEM: 2 x BM accumulators + 2 x 64 A columns <= 512
+    const int mt2 = (M + 191) / 192;
+    pl.bm = snap_bm((((M + mt2 - 1) / mt2) + 15) / 16 * 16);
+    if (pl.bm > 192) pl.bm = 192;
   }
   pl.m_tiles = (M + pl.bm - 1) / pl.bm;
   pl.n_tiles = (N + 128 * pl.nsub - 1) / (128 * pl.nsub);
@@ -702,7 +757,11 @@ int launch_nsub(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p,
     case 64: return launch_cfg<T, kInt8, NSUB, 64>(wm, xm, p, pl, s);
     case 128: return launch_cfg<T, kInt8, NSUB, 128>(wm, xm, p, pl, s);
     case 192: return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, s);
-    default: return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, s);
+    default:
+      // int8 with 256-row slabs caps the token tile at 192 (TMEM holds the
+      // accumulators and two widened A stages); the planner never asks more.
+      if constexpr (kInt8 && NSUB == 2) return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, s);
+      else return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, s);
   }
 }
 
@@ -722,8 +781,9 @@ extern "C" PS_API int ps_debug_tc_trace(unsigned long long* host, int n) {
 namespace ps_host {
 
 size_t linear_tc_workspace(int M, int N, int K) {
-  const Plan pl = plan(M, N, K);
-  return ws_bytes(pl, M, N);
+  const size_t a = ws_bytes(plan(M, N, K, true), M, N);
+  const size_t b = ws_bytes(plan(M, N, K, false), M, N);
+  return a > b ? a : b;
 }
 
 size_t tiled_int8_bytes(int N, int K) {
@@ -751,7 +811,7 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   if (K % 16 != 0 || !aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !aligned(resid, 16) ||
       !aligned(bias, 16) || !aligned(scale, 16) || !aligned(w_tiled, 16))
     return PS_ERR_UNSUPPORTED;
-  const Plan pl = plan(M, N, K);
+  const Plan pl = plan(M, N, K, int8);
   TcParams p{};
   p.wt = int8 ? w_tiled : nullptr;
   p.n_blocks = (N + 127) / 128;

@@ -332,12 +332,18 @@ def test_embedding_out_of_range_sets_device_status(dev):
 
 
 def _tile_ref(q):
-    """numpy restatement of the 8 KB-block layout [N/128][K/64][128][64]."""
+    """numpy restatement of the 8 KB-block layout [N/128][K/64][128][64] with
+    16-byte chunk c of row r stored in slot c ^ ((r >> 1) & 3)."""
     N, K = q.shape
     nb, kt = -(-N // 128), -(-K // 64)
     pad = np.zeros((nb * 128, kt * 64), np.int8)
     pad[:N, :K] = q
-    return pad.reshape(nb, 128, kt, 64).transpose(0, 2, 1, 3).reshape(-1)
+    blocks = pad.reshape(nb, 128, kt, 4, 16).transpose(0, 2, 1, 3, 4).copy()  # [nb][kt][r][c][16]
+    out = np.empty_like(blocks)
+    for r in range(128):
+        for c in range(4):
+            out[:, :, r, c ^ ((r >> 1) & 3)] = blocks[:, :, r, c]
+    return out.reshape(-1)
 
 
 @pytest.mark.parametrize("NK", [(136, 896), (300, 880), (2560, 2048)])
