@@ -116,13 +116,13 @@ PS_API int ps_paged_attention(void* out_dev, const void* q_dev, const void* k_ca
  * critical path where cudaMalloc's implicit synchronisation is not allowed).
  * Same inputs, outputs and semantics as ps_paged_attention, without the
  * workspace arguments: the split-context scratch is a static device array of
- * PS_ATTN_NOALLOC_SCRATCH_BYTES (16 MiB) that every GPU loading this library
+ * PS_ATTN_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU loading this library
  * holds until exit. A batch whose scratch need exceeds it is rejected with
  * PS_ERR_INVALID before any launch. The first call on a device looks up the
  * array's address (cudaGetSymbolAddress); make it before any stream capture.
  * Calls that overlap on the GPU share the array and race. Device-side range
  * errors skip the access but are not recorded in the status word. */
-#define PS_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define PS_ATTN_NOALLOC_SCRATCH_BYTES (8u << 20)
 PS_API int ps_paged_attention_noalloc(void* out_dev, const void* q_dev, const void* k_cache_dev,
                                       const void* v_cache_dev, const int32_t* block_tables_dev,
                                       int max_blocks_per_seq, const int32_t* cu_q_dev, const int32_t* start_pos_dev,

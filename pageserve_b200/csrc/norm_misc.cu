@@ -94,28 +94,55 @@ __global__ void embedding_kernel(T* __restrict__ out, const int64_t* __restrict_
 }
 
 // First index of the row maximum (torch.argmax semantics for finite input).
+// One CTA per row; 16-byte loads, four in flight per thread (the row is read
+// once, HBM bound), then a (value, index) tree reduction with first-index
+// tie-breaking.
+PS_DEVICE void argmax_merge(float& best, int& bidx, float ob, int oi) {
+  if (ob > best || (ob == best && oi < bidx)) {
+    best = ob;
+    bidx = oi;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(int32_t* __restrict__ out, const T* __restrict__ logits,
                                                       int V, int ld) {
+  constexpr int VEC = 16 / sizeof(T);
   const int row = blockIdx.x;
   const T* lr = logits + static_cast<long long>(row) * ld;
   float best = -FLT_MAX;
   int bidx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float f = to_f32(lr[i]);
-    if (f > best) {
-      best = f;
-      bidx = i;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(lr) % 16) == 0;
+  int tail = 0;
+  if (vec_ok) {
+    const int nv = V / VEC;
+    const uint4* lv = reinterpret_cast<const uint4*>(lr);
+    constexpr int U = 4;
+    for (int base = threadIdx.x; base < nv; base += blockDim.x * U) {
+      uint4 u[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int c = base + j * blockDim.x;
+        u[j] = c < nv ? __ldg(lv + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int c = base + j * blockDim.x;
+        if (c < nv) {
+          const T* e = reinterpret_cast<const T*>(&u[j]);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) argmax_merge(best, bidx, to_f32(e[i]), c * VEC + i);
+        }
+      }
     }
+    tail = nv * VEC;
   }
+  for (int i = tail + threadIdx.x; i < V; i += blockDim.x) argmax_merge(best, bidx, to_f32(lr[i]), i);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-    if (ob > best || (ob == best && oi < bidx)) {
-      best = ob;
-      bidx = oi;
-    }
+    argmax_merge(best, bidx, ob, oi);
   }
   __shared__ float sb[32];
   __shared__ int si[32];
@@ -133,10 +160,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(int32_t* __restrict__ out,
     for (int o = 16; o > 0; o >>= 1) {
       const float ob = __shfl_xor_sync(0xffffffffu, best, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-      if (ob > best || (ob == best && oi < bidx)) {
-        best = ob;
-        bidx = oi;
-      }
+      argmax_merge(best, bidx, ob, oi);
     }
     if (lane == 0) out[row] = bidx == 0x7fffffff ? 0 : bidx;
   }

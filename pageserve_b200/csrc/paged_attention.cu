@@ -17,7 +17,10 @@
 //   * PREFILL (T*G > 16 rows): each warp owns 16 rows; all warps share the
 //     key tiles; the causal bound stops each CTA at its last row's position.
 // The kernel is HBM bound: it reads each cached K/V row of the context once.
+#include <cudaTypedefs.h>
+
 #include <cfloat>
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -107,9 +110,24 @@ struct WarpState {
   float l[2];
 };
 
+PS_DEVICE void fence_proxy_async_a() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Shared-memory addressing of a K/V tile: row = key within the tile,
+// chunk = 16-byte column chunk (8 elements).
+template <int D>
+struct CpAsyncLayout {  // [key][D] rows, chunk ^ (row & 7) swizzle (cp.async staging)
+  static PS_DEVICE uint32_t addr(int row, int chunk) { return swz(row, chunk, D * 2); }
+};
+struct TmaLayout {  // D = 128 tiles of 16-key blocks, each as two 128B-swizzled [16 keys][64] halves (TMA)
+  static PS_DEVICE uint32_t addr(int row, int chunk) {
+    return static_cast<uint32_t>((row >> 4) * 4096 + (chunk >> 3) * 2048 + (row & 15) * 128 +
+                                 (((chunk & 7) ^ (row & 7)) << 4));
+  }
+};
+
 // Process one 16-key slab at tile row `kr0` (key positions kp0..kp0+15).
 // row_limit[i] = last key position row i may attend (causal), or -1.
-template <typename T, int D>
+template <typename T, int D, typename Layout = CpAsyncLayout<D>>
 PS_DEVICE void process_slab(WarpState<D>& st, const uint32_t (*qa)[4], uint32_t k_smem, uint32_t v_smem, int kr0,
                             int kp0, const int row_limit[2], float scale_log2) {
   const int lane = threadIdx.x & 31;
@@ -125,7 +143,7 @@ PS_DEVICE void process_slab(WarpState<D>& st, const uint32_t (*qa)[4], uint32_t 
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
       uint32_t b[4];
-      ldmatrix_x4(k_smem + swz(krow, 2 * ks + (mat & 1), D * 2), b[0], b[1], b[2], b[3]);
+      ldmatrix_x4(k_smem + Layout::addr(krow, 2 * ks + (mat & 1)), b[0], b[1], b[2], b[3]);
       mma_16816<T>(s[0], qa[ks], b);
       mma_16816<T>(s[1], qa[ks], b + 2);
     }
@@ -190,7 +208,89 @@ PS_DEVICE void process_slab(WarpState<D>& st, const uint32_t (*qa)[4], uint32_t 
 #pragma unroll
     for (int dp = 0; dp < D / 16; ++dp) {
       uint32_t b[4];
-      ldmatrix_x4_trans(v_smem + swz(vrow, 2 * dp + (mat >> 1), D * 2), b[0], b[1], b[2], b[3]);
+      ldmatrix_x4_trans(v_smem + Layout::addr(vrow, 2 * dp + (mat >> 1)), b[0], b[1], b[2], b[3]);
+      mma_16816<T>(st.o[2 * dp], pa, b);
+      mma_16816<T>(st.o[2 * dp + 1], pa, b + 2);
+    }
+  }
+}
+
+// Prefill step: 16 query rows against the whole 64-key tile at once (one
+// online-softmax update and one rescale of O per 64 keys instead of four).
+// masked = false when every key of the tile is visible to every valid row.
+template <typename T, int D, typename Layout = CpAsyncLayout<D>>
+PS_DEVICE void process_tile64(WarpState<D>& st, const uint32_t (*qa)[4], uint32_t k_smem, uint32_t v_smem, int kp0,
+                              const int row_limit[2], float scale_log2, bool masked) {
+  const int lane = threadIdx.x & 31;
+  const int mat = lane >> 3;
+  float s[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t b[4];
+      const int krow = np * 16 + ((mat >> 1) << 3) + (lane & 7);
+      ldmatrix_x4(k_smem + Layout::addr(krow, 2 * ks + (mat & 1)), b[0], b[1], b[2], b[3]);
+      mma_16816<T>(s[2 * np], qa[ks], b);
+      mma_16816<T>(s[2 * np + 1], qa[ks], b + 2);
+    }
+  }
+  float mt[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int ri = e >> 1;
+      const int kp = kp0 + n * 8 + 2 * (lane & 3) + (e & 1);
+      if (!masked || kp <= row_limit[ri]) {
+        s[n][e] *= scale_log2;
+        mt[ri] = fmaxf(mt[ri], s[n][e]);
+      } else {
+        s[n][e] = -INFINITY;
+      }
+    }
+  float corr[2];
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) {
+    mt[ri] = fmaxf(mt[ri], __shfl_xor_sync(0xffffffffu, mt[ri], 1));
+    mt[ri] = fmaxf(mt[ri], __shfl_xor_sync(0xffffffffu, mt[ri], 2));
+    const float mn = fmaxf(st.m[ri], mt[ri]);
+    corr[ri] = exp2f(st.m[ri] - mn);
+    st.m[ri] = mn;
+  }
+  float rs[2] = {0.f, 0.f};
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      s[n][e] = exp2f(s[n][e] - st.m[e >> 1]);
+      rs[e >> 1] += s[n][e];
+    }
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) st.l[ri] = st.l[ri] * corr[ri] + rs[ri];
+#pragma unroll
+  for (int dt = 0; dt < D / 8; ++dt) {
+    st.o[dt][0] *= corr[0];
+    st.o[dt][1] *= corr[0];
+    st.o[dt][2] *= corr[1];
+    st.o[dt][3] *= corr[1];
+  }
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    uint32_t pa[4];
+    pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+    pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+    pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+    const int vrow = kk * 16 + ((mat & 1) << 3) + (lane & 7);
+#pragma unroll
+    for (int dp = 0; dp < D / 16; ++dp) {
+      uint32_t b[4];
+      ldmatrix_x4_trans(v_smem + Layout::addr(vrow, 2 * dp + (mat >> 1)), b[0], b[1], b[2], b[3]);
       mma_16816<T>(st.o[2 * dp], pa, b);
       mma_16816<T>(st.o[2 * dp + 1], pa, b + 2);
     }
@@ -249,11 +349,17 @@ __global__ void __launch_bounds__(kThreads) paged_attention_kernel(const AttnPar
       return;
     }
   } else {
-    row0 = blockIdx.x * 64;
+    // blockIdx.x = (row tile, key split); the last rows (longest causal key
+    // ranges) come first so the tail of the grid is short.
+    const int ntile = (gridDim.x + p.num_splits - 1) / p.num_splits;
+    const int rt = ntile - 1 - static_cast<int>(blockIdx.x) / p.num_splits;
+    const int split = static_cast<int>(blockIdx.x) % p.num_splits;
+    row0 = rt * 64;
     if (row0 >= R) return;
     const int last_row = min(R, row0 + 64) - 1;
-    kv_begin = 0;
-    kv_end = min(ctx, sp + last_row / p.G + 1);
+    kv_begin = split * p.split_tokens;
+    kv_end = min(min(ctx, sp + last_row / p.G + 1), kv_begin + p.split_tokens);
+    if (kv_begin >= kv_end) return;
   }
   const int warp_row0 = DECODE ? row0 : row0 + warp * 16;
 
@@ -303,11 +409,10 @@ __global__ void __launch_bounds__(kThreads) paged_attention_kernel(const AttnPar
       if (kp0 <= lim) process_slab<T, D>(st, qa, ks, vs, warp * 16, kp0, row_limit, p.scale_log2);
     } else {
       const int lim = __reduce_max_sync(0xffffffffu, warp_max_row_limit);
-#pragma unroll
-      for (int sl = 0; sl < kKT / 16; ++sl) {
-        const int kp0 = t0 + sl * 16;
-        if (kp0 <= lim) process_slab<T, D>(st, qa, ks, vs, sl * 16, kp0, row_limit, p.scale_log2);
-      }
+      // every valid row sees the whole tile: no per-key masking needed
+      const int vis = __reduce_min_sync(0xffffffffu, min(row_limit[0] < 0 ? INT_MAX : row_limit[0],
+                                                         row_limit[1] < 0 ? INT_MAX : row_limit[1]));
+      if (t0 <= lim) process_tile64<T, D>(st, qa, ks, vs, t0, row_limit, p.scale_log2, t0 + kKT - 1 > vis);
     }
   }
   cp_async_wait<0>();
@@ -322,16 +427,29 @@ __global__ void __launch_bounds__(kThreads) paged_attention_kernel(const AttnPar
 
   if (!DECODE) {
     T* out = static_cast<T*>(p.out);
+    const int split = static_cast<int>(blockIdx.x) % p.num_splits;
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int r = warp_row0 + (lane >> 2) + hf * 8;
       if (r >= R) continue;
       const float inv = st.l[hf] > 0.f ? 1.f / st.l[hf] : 0.f;
-      T* dst = out + (static_cast<long long>(q0 + r / p.G) * p.Hq + h * p.G + r % p.G) * D;
+      const int t = r / p.G, g = r % p.G;
+      if (p.num_splits == 1) {
+        T* dst = out + (static_cast<long long>(q0 + t) * p.Hq + h * p.G + g) * D;
 #pragma unroll
-      for (int dt = 0; dt < D / 8; ++dt) {
-        const int d = dt * 8 + 2 * (lane & 3);
-        *reinterpret_cast<uint32_t*>(dst + d) = pack2<T>(st.o[dt][2 * hf] * inv, st.o[dt][2 * hf + 1] * inv);
+        for (int dt = 0; dt < D / 8; ++dt) {
+          const int d = dt * 8 + 2 * (lane & 3);
+          *reinterpret_cast<uint32_t*>(dst + d) = pack2<T>(st.o[dt][2 * hf] * inv, st.o[dt][2 * hf + 1] * inv);
+        }
+      } else {
+        const long long prow = (static_cast<long long>(b) * p.num_splits + split) * p.rows_max + t * p.Hq + h * p.G + g;
+        float* dst = p.o_part + prow * D;
+#pragma unroll
+        for (int dt = 0; dt < D / 8; ++dt) {
+          const int d = dt * 8 + 2 * (lane & 3);
+          *reinterpret_cast<float2*>(dst + d) = make_float2(st.o[dt][2 * hf] * inv, st.o[dt][2 * hf + 1] * inv);
+        }
+        if ((lane & 3) == 0) p.lse_part[prow] = st.l[hf] > 0.f ? st.m[hf] + log2f(st.l[hf]) : -FLT_MAX;
       }
     }
     return;
@@ -401,6 +519,255 @@ __global__ void __launch_bounds__(kThreads) paged_attention_kernel(const AttnPar
   }
 }
 
+// ---------------------------------------------------------------------------
+// TMA-fed decode kernel for the serving shape (head_dim 128, block size 16).
+// CTA = (context split, kv head, sequence), 5 warps: warp 0 produces, warps
+// 1..4 consume. The producer looks up each 16-key block of a 64-key tile in
+// the block table and issues 3-D TMA loads (box: 64 dims x 1 head x 16 keys,
+// 128B swizzle) of its K and V halves into a 3-stage mbarrier ring; consumer
+// warp w owns block w-1 of every tile (one 16-key mma.sync slab). Loads are
+// a handful of instructions per 8 KB, so the ring keeps ~2 tiles per CTA (2
+// CTAs per SM) in flight.
+constexpr int kTmaStages = 3;
+constexpr int kTmaTile = 64;
+constexpr int kTmaStageBytes = 2 * kTmaTile * 128 * 2;  // K + V, 32 KB
+constexpr long long kAttnWaitCycles = 2000000000LL;
+
+PS_DEVICE void mbar_init_a(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+PS_DEVICE void mbar_expect_tx_a(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+PS_DEVICE void mbar_arrive_a(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+PS_DEVICE bool mbar_try_wait_a(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded warp-uniform wait (about a second): false on timeout or abort.
+PS_DEVICE bool warp_wait_a(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  bool ok = true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_a(bar, parity)) {
+    if (*abort_flag) {
+      ok = false;
+      break;
+    }
+    if (clock64() - t0 > kAttnWaitCycles) {
+      *abort_flag = 1;
+      record_error(status, kErrTimeout);
+      ok = false;
+      break;
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+PS_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                         const __grid_constant__ CUtensorMap vmap,
+                                                         const AttnParams p) {
+  constexpr int D = 128;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + kTmaStages * kTmaStageBytes;
+  auto full = [&](int s) { return bars + 8 * s; };
+  auto empty = [&](int s) { return bars + 8 * (kTmaStages + s); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kTmaStages * kTmaStageBytes + 8 * 2 * kTmaStages);
+
+  const int b = blockIdx.z;
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q0 = p.cu_q[b];
+  const int T_b = p.cu_q[b + 1] - q0;
+  const int sp = p.start_pos[b];
+  const int ctx = sp + T_b;
+  const int R = T_b * p.G;
+  const int32_t* table = p.tables + static_cast<long long>(b) * p.max_blocks;
+  if (T_b <= 0) return;
+  if (T_b > p.max_q_len || ctx > p.max_ctx || sp < 0 || ctx > p.max_blocks * p.block_size || R > 16) {
+    if (threadIdx.x == 0) record_error(p.status, kErrShape);
+    return;
+  }
+  const int kv_begin = blockIdx.x * p.split_tokens;
+  if (kv_begin >= ctx) return;
+  const int kv_end = min(ctx, kv_begin + p.split_tokens);
+  const int ntiles = (kv_end - kv_begin + kTmaTile - 1) / kTmaTile;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kTmaStages; ++s) {
+      mbar_init_a(full(s), 1);
+      mbar_init_a(empty(s), 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  WarpState<D> st;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % kTmaStages;
+      if (i >= kTmaStages && !warp_wait_a(empty(s), ((i / kTmaStages) - 1) & 1, abort_flag, p.status)) break;
+      if (lane == 0) {
+        const int t0 = kv_begin + i * kTmaTile;
+        const int nblk = min(4, (kv_end - t0 + 15) / 16);
+        mbar_expect_tx_a(full(s), nblk * 4 * 2048);
+        const uint32_t kst = base + s * kTmaStageBytes;
+        const uint32_t vst = kst + kTmaStageBytes / 2;
+        for (int j = 0; j < nblk; ++j) {
+          int phys = table[(t0 + 16 * j) / 16];
+          if (phys < 0 || phys >= p.num_blocks) {
+            record_error(p.status, kErrBlockId);
+            phys = 0;  // keep the transaction count; the output is flagged invalid
+          }
+          const int row = phys * 16;
+          tma_load_3d(kst + j * 4096, &kmap, full(s), 0, h, row);
+          tma_load_3d(kst + j * 4096 + 2048, &kmap, full(s), 64, h, row);
+          tma_load_3d(vst + j * 4096, &vmap, full(s), 0, h, row);
+          tma_load_3d(vst + j * 4096 + 2048, &vmap, full(s), 64, h, row);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ consumers --
+    const int cw = warp - 1;  // which 16-key block of each tile
+    uint32_t qa[D / 16][4];
+    load_q<T, D>(qa, p, q0, h, 0, R);
+    int row_limit[2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = (lane >> 2) + hf * 8;
+      row_limit[hf] = r < R ? min(sp + r / p.G, kv_end - 1) : -1;
+    }
+    const int lim = __reduce_max_sync(0xffffffffu, max(row_limit[0], row_limit[1]));
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st.o[dt][e] = 0.f;
+    st.m[0] = st.m[1] = -FLT_MAX;
+    st.l[0] = st.l[1] = 0.f;
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % kTmaStages;
+      if (!warp_wait_a(full(s), (i / kTmaStages) & 1, abort_flag, p.status)) break;
+      const uint32_t kst = base + s * kTmaStageBytes;
+      const uint32_t vst = kst + kTmaStageBytes / 2;
+      const int kp0 = kv_begin + i * kTmaTile + cw * 16;
+      if (kp0 < kv_end && kp0 <= lim) {
+        const int valid = kv_end - kp0;
+        if (valid < 16) {
+          // zero the V rows past the context so 0-probability keys add 0
+          unsigned char* vb = gbase + (vst - base) + cw * 4096;
+          for (int u = lane; u < (16 - valid) * 16; u += 32) {
+            const int row = valid + u / 16, part = u % 16;
+            *reinterpret_cast<uint4*>(vb + (part >> 3) * 2048 + row * 128 + ((part & 7) << 4)) =
+                make_uint4(0, 0, 0, 0);
+          }
+          __syncwarp();
+        }
+        process_slab<T, D, TmaLayout>(st, qa, kst, vst, cw * 16, kp0, row_limit, p.scale_log2);
+        if (valid < 16) fence_proxy_async_a();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_a(empty(s));
+    }
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      st.l[ri] += __shfl_xor_sync(0xffffffffu, st.l[ri], 1);
+      st.l[ri] += __shfl_xor_sync(0xffffffffu, st.l[ri], 2);
+    }
+  }
+  __syncthreads();  // every TMA consumed: the stage memory is free for the merge
+
+  // Merge the 4 consumer warps' states (same as the cp.async decode kernel).
+  float* sm_o = reinterpret_cast<float*>(gbase);  // [4][16][D]
+  float* sm_m = sm_o + 4 * 16 * D;
+  float* sm_l = sm_m + 4 * 16;
+  if (warp > 0) {
+    const int cw = warp - 1;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = (lane >> 2) + hf * 8;
+      float* orow = sm_o + (cw * 16 + r) * D;
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        const int d = dt * 8 + 2 * (lane & 3);
+        *reinterpret_cast<float2*>(orow + d) = make_float2(st.o[dt][2 * hf], st.o[dt][2 * hf + 1]);
+      }
+      if ((lane & 3) == 0) {
+        sm_m[cw * 16 + r] = st.m[hf];
+        sm_l[cw * 16 + r] = st.l[hf];
+      }
+    }
+  }
+  __syncthreads();
+  if (warp > 0) {
+    const int ct = threadIdx.x - 32;
+    const int r = ct >> 3;
+    const int part = ct & 7;
+    if (r < R) {
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) mx = fmaxf(mx, sm_m[w * 16 + r]);
+      float wgt[4];
+      float l = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        wgt[w] = exp2f(sm_m[w * 16 + r] - mx);
+        l += sm_l[w * 16 + r] * wgt[w];
+      }
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      constexpr int DP = D / 8;
+      float acc[DP];
+#pragma unroll
+      for (int i2 = 0; i2 < DP; ++i2) acc[i2] = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float* orow = sm_o + (w * 16 + r) * D + part * DP;
+#pragma unroll
+        for (int i2 = 0; i2 < DP; ++i2) acc[i2] += orow[i2] * wgt[w];
+      }
+      const int t = r / p.G, g = r % p.G;
+      if (p.num_splits == 1) {
+        T* dst = static_cast<T*>(p.out) + (static_cast<long long>(q0 + t) * p.Hq + h * p.G + g) * D + part * DP;
+#pragma unroll
+        for (int i2 = 0; i2 < DP; i2 += 2)
+          *reinterpret_cast<uint32_t*>(dst + i2) = pack2<T>(acc[i2] * inv, acc[i2 + 1] * inv);
+      } else {
+        const long long prow =
+            (static_cast<long long>(b) * p.num_splits + blockIdx.x) * p.rows_max + t * p.Hq + h * p.G + g;
+        float* dst = p.o_part + prow * D + part * DP;
+#pragma unroll
+        for (int i2 = 0; i2 < DP; i2 += 4)
+          *reinterpret_cast<float4*>(dst + i2) =
+              make_float4(acc[i2] * inv, acc[i2 + 1] * inv, acc[i2 + 2] * inv, acc[i2 + 3] * inv);
+        if (part == 0) p.lse_part[prow] = l > 0.f ? mx + log2f(l) : -FLT_MAX;
+      }
+    }
+  }
+}
+
 // Merge split partials: one warp per (sequence, chunk token, q head) row.
 template <typename T, int D>
 __global__ void combine_kernel(const AttnParams p) {
@@ -412,7 +779,10 @@ __global__ void combine_kernel(const AttnParams p) {
   const int lane = threadIdx.x & 31;
   if (T_b > p.max_q_len || ctx > p.max_ctx) return;  // the attention kernel recorded the error
   if (row >= T_b * p.Hq) return;
-  const int nsplit = min(p.num_splits, (ctx + p.split_tokens - 1) / p.split_tokens);
+  // splits that saw this row's keys: positions 0 .. start_pos + t (causal)
+  const int last_key = p.start_pos[b] + row / p.Hq;
+  const int nsplit = min(p.num_splits, last_key / p.split_tokens + 1);
+  (void)ctx;
   const long long base = static_cast<long long>(b) * p.num_splits * p.rows_max + row;
   float mx = -FLT_MAX;
   for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.lse_part[base + static_cast<long long>(s) * p.rows_max]);
@@ -439,13 +809,34 @@ __global__ void combine_kernel(const AttnParams p) {
 // Split heuristic shared by the workspace query and the launch: split the
 // context when (sequences x kv heads) CTAs cannot fill the 148 SMs a few
 // times over.
-void plan_splits(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int* num_splits, int* split_tokens) {
+void plan_splits(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int D, int* num_splits,
+                 int* split_tokens, size_t max_ws = ~static_cast<size_t>(0)) {
   const int G = Hq / Hkv;
   *num_splits = 1;
   *split_tokens = max_ctx > 0 ? max_ctx : 1;
-  if (max_q_len * G > 16) return;  // prefill kernel: no split
+  if (max_q_len * G > 16) {
+    // Prefill tiles (64 query rows) over the causal key range: split the key
+    // range into 128-key pieces when the tiles alone give under ~3 CTAs per
+    // SM (one warp per SM sub-partition leaves every mma.sync stall exposed),
+    // as long as the (o, lse) partials fit the workspace cap.
+    const long long base = static_cast<long long>((max_q_len * G + 63) / 64) * Hkv * num_seqs;
+    int splits = static_cast<int>((3LL * 148 + base - 1) / base);
+    const int max_by_len = (max_ctx + 127) / 128;
+    if (splits > max_by_len) splits = max_by_len;
+    while (splits > 1 &&
+           static_cast<size_t>(num_seqs) * splits * max_q_len * Hq * (D + 1) * sizeof(float) + 256 > max_ws)
+      --splits;
+    if (splits <= 1) return;
+    int st = (max_ctx + splits - 1) / splits;
+    st = (st + kKT - 1) / kKT * kKT;
+    *split_tokens = st;
+    *num_splits = (max_ctx + st - 1) / st;
+    return;
+  }
   const long long ctas = static_cast<long long>(num_seqs) * Hkv;
-  const long long target = 148LL * 3 * 4;
+  // head_dim 128 runs the TMA kernel (2 CTAs per SM with a deep ring): about
+  // 1.5 waves of long splits; the cp.async kernel wants many short ones.
+  const long long target = D == 128 ? 148LL * 2 * 3 / 2 : 148LL * 3 * 4;
   int splits = static_cast<int>((target + ctas - 1) / ctas);
   const int max_by_len = (max_ctx + 255) / 256;  // at least 256 keys per split
   if (splits > max_by_len) splits = max_by_len;
@@ -458,15 +849,78 @@ void plan_splits(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int*
 
 size_t workspace_bytes_for(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int D) {
   int ns, st;
-  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, &ns, &st);
+  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, D, &ns, &st);
   if (ns <= 1) return 0;
   const size_t rows = static_cast<size_t>(num_seqs) * ns * max_q_len * Hq;
   return rows * D * sizeof(float) + rows * sizeof(float) + 256;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// One layer's cache as a 3-D tensor [num_blocks*16 keys][Hkv][128] with a
+// 64 x 1 x 16 box (one half of one head's 16-key block), 128B swizzle.
+bool make_kv_map(CUtensorMap* map, const void* cache, bool bf16, int num_blocks, int Hkv) {
+  auto fn = attn_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(Hkv), static_cast<cuuint64_t>(num_blocks) * 16};
+  cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(Hkv) * 128 * 2};
+  cuuint32_t box[3] = {64, 1, 16};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+            const_cast<void*>(cache), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+int launch_decode_tma(AttnParams& p, int num_seqs, int max_q_len, cudaStream_t s) {
+  CUtensorMap km, vm;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (!make_kv_map(&km, p.k_cache, bf16, p.num_blocks, p.Hkv) || !make_kv_map(&vm, p.v_cache, bf16, p.num_blocks, p.Hkv)) {
+    ps_host::set_error("paged_attention: cuTensorMapEncodeTiled failed for the KV cache");
+    return PS_ERR_CUDA;
+  }
+  const int smem = kTmaStages * kTmaStageBytes + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(decode_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      ps_host::set_error("paged_attention: cannot reserve %d bytes of shared memory", smem);
+      return PS_ERR_CUDA;
+    }
+    attr = true;
+  }
+  dim3 grid(p.num_splits, p.Hkv, num_seqs);
+  decode_tma_kernel<T><<<grid, 160, smem, s>>>(km, vm, p);
+  ps_host::count_launch();
+  int rc = ps_host::check_launch("paged_attention(decode, tma)");
+  if (rc != PS_OK || p.num_splits == 1) return rc;
+  const int rows = max_q_len * p.Hq;
+  dim3 cgrid((rows + 3) / 4, num_seqs);
+  combine_kernel<T, 128><<<cgrid, 128, 0, s>>>(p);
+  ps_host::count_launch();
+  return ps_host::check_launch("paged_attention(combine)");
+}
+
 template <typename T, int D>
 int launch(AttnParams& p, int num_seqs, int max_q_len, int max_ctx, cudaStream_t s) {
   const bool decode = max_q_len * p.G <= 16;
+  if constexpr (D == 128) {
+    // the serving layout: TMA needs 16-key blocks and 16-byte aligned rows
+    if (decode && p.block_size == 16 && static_cast<long long>(p.num_blocks) * 16 < (1LL << 31) &&
+        ps_host::aligned(p.k_cache, 16) && ps_host::aligned(p.v_cache, 16))
+      return launch_decode_tma<T>(p, num_seqs, max_q_len, s);
+  }
   const int stage_smem = kStages * 2 * Tile<D>::kBytes;
   const int merge_smem = kWarps * 16 * D * 4 + 2 * kWarps * 16 * 4;
   const int smem = stage_smem > merge_smem ? stage_smem : merge_smem;
@@ -486,10 +940,16 @@ int launch(AttnParams& p, int num_seqs, int max_q_len, int max_ctx, cudaStream_t
   }
   auto kern = paged_attention_kernel<T, D, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  dim3 grid((max_q_len * p.G + 63) / 64, p.Hkv, num_seqs);
+  dim3 grid(((max_q_len * p.G + 63) / 64) * p.num_splits, p.Hkv, num_seqs);
   kern<<<grid, kThreads, smem, s>>>(p);
   ps_host::count_launch();
-  return ps_host::check_launch("paged_attention(prefill)");
+  int rc = ps_host::check_launch("paged_attention(prefill)");
+  if (rc != PS_OK || p.num_splits == 1) return rc;
+  const int rows = max_q_len * p.Hq;
+  dim3 cgrid((rows + 3) / 4, num_seqs);
+  combine_kernel<T, D><<<cgrid, 128, 0, s>>>(p);
+  ps_host::count_launch();
+  return ps_host::check_launch("paged_attention(prefill combine)");
 }
 
 }  // namespace
@@ -549,7 +1009,7 @@ int ps_paged_attention(void* out, const void* q, const void* k_cache, const void
   p.max_q_len = max_q_len;
   p.max_ctx = max_ctx;
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * kLog2e;
-  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, &p.num_splits, &p.split_tokens);
+  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, D, &p.num_splits, &p.split_tokens);
   if (p.num_splits > 1) {
     const size_t need = workspace_bytes_for(num_seqs, max_q_len, max_ctx, Hq, Hkv, D);
     if (!workspace || workspace_bytes < need) {
@@ -655,7 +1115,8 @@ extern "C" int ps_paged_attention_noalloc(void* out, const void* q, const void* 
     ps_host::set_error("paged_attention_noalloc: caches need 16-byte, q/out 4-byte alignment");
     return PS_ERR_INVALID;
   }
-  const size_t need = workspace_bytes_for(num_seqs, max_q_len, max_ctx, Hq, Hkv, D);
+  const bool prefill = max_q_len * (Hq / Hkv) > 16;  // prefill splits shrink to fit the static scratch
+  const size_t need = prefill ? 0 : workspace_bytes_for(num_seqs, max_q_len, max_ctx, Hq, Hkv, D);
   if (need > PS_ATTN_NOALLOC_SCRATCH_BYTES) {
     ps_host::set_error(
         "paged_attention_noalloc: this batch needs %zu bytes of split scratch, above the static limit of %zu "
@@ -683,7 +1144,8 @@ extern "C" int ps_paged_attention_noalloc(void* out, const void* q, const void* 
   p.max_q_len = max_q_len;
   p.max_ctx = max_ctx;
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * kLog2e;
-  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, &p.num_splits, &p.split_tokens);
+  plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, D, &p.num_splits, &p.split_tokens,
+              PS_ATTN_NOALLOC_SCRATCH_BYTES);
   if (p.num_splits > 1) {
     void* scratch = nullptr;
     const int rc = noalloc_scratch(&scratch);

@@ -141,13 +141,35 @@ def bench_attn(B=64, lo=512, hi=4096, Hq=16, Hkv=2, D=128, bs=16, pool=20000, it
             "frac": byts / ms / 1e6 / hbm, "ideal_us": byts / (hbm * 1e9) * 1e6}
 
 
+def bench_attn_prefill(T=512, start=0, Hq=16, Hkv=2, D=128, bs=16, iters=20, seed=0, warmup=3):
+    """One causal prefill chunk of T tokens at ``start`` (the config-4 chunk)."""
+    from .paged_attention import AttentionWorkspace, paged_attention
+    dev = torch.device("cuda")
+    ctx = start + T
+    nblk = (ctx + bs - 1) // bs
+    pool = max(4 * nblk, 64)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    kc = torch.randn(pool, bs, Hkv, D, device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(pool, bs, Hkv, D, device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(T, Hq, D, device=dev, generator=g, dtype=torch.bfloat16)
+    tab = torch.randperm(pool, device=dev)[:nblk].to(torch.int32).reshape(1, -1)
+    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    sp = torch.tensor([start], dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    aws = AttentionWorkspace()
+    ms = _time(lambda: paged_attention(q, kc, vc, tab, cu, sp, T, ctx, out=out, workspace=aws), iters, warmup)
+    flops = 4.0 * Hq * D * sum(start + i + 1 for i in range(T))
+    return {"case": "attn_prefill", "T": T, "start": start, "us": ms * 1e3, "tflops": flops / ms / 1e9}
+
+
 SWEEP_NK = [(2560, 2048), (2048, 2048), (22016, 2048), (2048, 11008)]
 SWEEP_M = [1, 8, 64, 256, 2048]
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["linear", "sweep", "attn"])
+    ap.add_argument("what", choices=["linear", "sweep", "attn", "prefill"])
     ap.add_argument("--M", type=int, default=576)
     ap.add_argument("--N", type=int, default=22016)
     ap.add_argument("--K", type=int, default=2048)
@@ -164,6 +186,8 @@ def main(argv=None):
         for n, k in SWEEP_NK:
             for m in SWEEP_M:
                 print(json.dumps(bench_linear(m, n, k, a.iters, warmup=a.warmup, tiled=not a.row_major)), flush=True)
+    elif a.what == "prefill":
+        print(json.dumps(bench_attn_prefill(iters=a.iters, warmup=a.warmup)))
     else:
         print(json.dumps(bench_attn(iters=a.iters, warmup=a.warmup)))
     from . import _lib

@@ -22,7 +22,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 REL_TOL = 2e-2  # the bf16 tolerance used by the other GPU tests
-NOALLOC_LIMIT = 16 << 20  # PS_ATTN_NOALLOC_SCRATCH_BYTES in include/pageserve_b200.h
+NOALLOC_LIMIT = 8 << 20  # PS_ATTN_NOALLOC_SCRATCH_BYTES in include/pageserve_b200.h
 
 
 def rel_err(a, b):
@@ -87,11 +87,14 @@ def test_noalloc_rejects_batches_above_the_static_scratch():
     if not _lib.LIB_PATH.exists():
         pytest.skip("library not built")
     lib = _lib.load()
-    # 64 sequences x 2 query tokens x 64 heads at context 4096 need ~16.9 MB of partials
-    need = lib.ps_paged_attention_workspace_size(64, 2, 4096, 64, 8, 128)
+    # A decode batch whose split partials exceed the static scratch: 275
+    # sequences x 2 query tokens x 32 heads (8 per kv head) at head_dim 64.
+    args = (275, 2, 4096, 32, 4, 64)  # seqs, max_q_len, max_ctx, q heads, kv heads, head_dim
+    need = lib.ps_paged_attention_workspace_size(*args)
     assert need > NOALLOC_LIMIT
     fake = 1 << 20  # never dereferenced: the size check runs before any device access
-    rc = lib.ps_paged_attention_noalloc(fake, fake, fake, fake, fake, 256, fake, fake, 64, 128, 2, 4096, 1024, 16,
-                                        64, 8, 128, _lib.PS_BF16, None)
+    seqs, qlen, ctx, hq, hkv, d = args
+    rc = lib.ps_paged_attention_noalloc(fake, fake, fake, fake, fake, 256, fake, fake, seqs, seqs * qlen, qlen, ctx,
+                                        4096, 16, hq, hkv, d, _lib.PS_BF16, None)
     assert rc == _lib.PS_ERR_INVALID
     assert "static limit" in _lib.last_error()
