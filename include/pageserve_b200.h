@@ -208,6 +208,57 @@ PS_API int ps_embedding(void* out_dev, const int64_t* ids_dev, const void* table
  * the maximum of each row; logits (M, V) in dtype; out int32 [M]. */
 PS_API int ps_argmax(int32_t* out_dev, const void* logits_dev, int M, int V, int ld, int dtype, ps_stream_t stream);
 
+/* ------------------------------------- (e) fused tensor-parallel all-reduce
+ *
+ * Replaces the dist.all_reduce(partial, SUM) after each row-parallel linear
+ * (engine/tensor_parallel.py:34-48, called for o_proj and down_proj) with a
+ * push over peer memory: the linear's final writer stores its output tile
+ * into every rank's receive buffer, and the next RMSNorm sums the ranks'
+ * slots. One process per GPU; buffers are shared through CUDA IPC.
+ *
+ * Receive buffer (one per rank, zeroed by ps_comm_alloc):
+ *   bytes [0, PS_COMM_CTRL_BYTES): u32 control words; set s in {0, 1} has its
+ *     arrival flag at 4*s (written by every rank's producer), its consumed
+ *     counter at 64 + 4*s and its producer CTA counter at 128 + 4*s (local);
+ *   then slots [2 sets][world][max_tokens][hidden] of dtype.
+ * The two sets alternate (o_proj -> set 0, down_proj -> set 1). Every wait is
+ * bounded (a few seconds); on timeout PS_ERR_TIMEOUT-style code 4 is recorded
+ * in the device status word (ps_device_status) and the kernel finishes. */
+#define PS_COMM_CTRL_BYTES 1024
+#define PS_COMM_MAX_WORLD 8
+
+PS_API size_t ps_comm_buffer_bytes(int world, int max_tokens, int hidden, int dtype);
+/* cudaMalloc + zero fill (IPC-shareable device memory). */
+PS_API int ps_comm_alloc(void** buf_dev, size_t bytes);
+PS_API int ps_comm_free(void* buf_dev);
+/* cudaIpcGetMemHandle / cudaIpcOpenMemHandle on 64-byte opaque handles. */
+PS_API int ps_ipc_get_handle(void* buf_dev, void* handle64_out);
+PS_API int ps_ipc_open_handle(const void* handle64, void** peer_buf_out);
+PS_API int ps_ipc_close(void* peer_buf);
+
+/* Row-parallel linear with push (tensor_parallel.py:34-46, the local
+ * product partial = x_shard @ W_shard.T): y = x @ W.T (* scale for int8 W,
+ * per output row; no bias), M tokens, N = hidden, K = this rank's input
+ * shard. Instead of a local output, every rank r's slot [set][rank] gets the
+ * (M, N) result (rank_bufs[r]: rank r's receive buffer as mapped in this
+ * process, rank_bufs[rank] this rank's own), then every rank's flag of `set`
+ * is raised by one. Weight as ps_w8a16_linear_tiled (w_tiled != NULL, int8)
+ * or ps_linear (16-bit W, w_tiled NULL); always the tensor-core kernel;
+ * workspace from ps_w8a16_linear_tiled_workspace_size. */
+PS_API int ps_linear_push(const void* x_dev, const void* w_dev, int wdtype, const int8_t* w_tiled_dev,
+                          const float* scale_dev, int M, int N, int K, int dtype, void* const* rank_bufs, int world,
+                          int rank, int set, int max_tokens, void* workspace_dev, size_t workspace_bytes,
+                          ps_stream_t stream);
+
+/* The consumer (tensor_parallel.py:47 + engine/model.py:184-190): waits until
+ * `set`'s flag in this rank's buffer shows all `world` ranks, s = sum over
+ * ranks of the slots (float32, rank order, rounded to dtype like the reduced
+ * linear output). With weight_dev != NULL: x = x + s (rounded to dtype, in
+ * place) and y = rmsnorm(x) * weight (ps_rmsnorm's math); with weight_dev
+ * NULL: y = s (the plain all-reduce result; x unused). Re-arms the set. */
+PS_API int ps_allreduce_rmsnorm(void* y_dev, void* x_dev, const void* weight_dev, float eps, int M, int H,
+                                int dtype, void* buf_dev, int world, int set, int max_tokens, ps_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

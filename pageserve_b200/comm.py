@@ -1,0 +1,166 @@
+"""Fused tensor-parallel all-reduce over peer memory (the B200 replacement of
+the ``dist.all_reduce(partial, SUM)`` in engine/tensor_parallel.py:34-48).
+
+Each rank allocates one receive buffer (``ps_comm_alloc``) and maps every
+peer's buffer into its own address space through CUDA IPC handles exchanged
+with ``torch.distributed`` (one ``all_gather_object`` at setup). Then, per
+row-parallel linear:
+
+  ``linear_push(x_shard, weight, set)``   the tensor-core linear whose final
+      writer stores its (tokens, hidden) output into slot[rank] of every
+      rank's buffer and raises every rank's arrival flag of ``set``;
+  ``allreduce_rmsnorm(x, w, eps, set)``   waits for all ranks' slots, sums
+      them, adds the residual x (in place) and returns rmsnorm(x) * w —
+      or, with ``w=None``, returns the plain reduced sum.
+
+The two slot sets alternate between the o_proj (set 0) and down_proj
+(set 1) reductions of a layer. ``FusedAllReduce.emulated`` builds the W
+ranks' buffers in one process on one GPU (every rank's kernels issued in
+sequence on one stream), which exercises the same kernels and flags
+without a second GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+HANDLE_BYTES = 64
+
+
+class FusedAllReduce:
+    """One rank's receive buffer plus every rank's buffer as mapped here."""
+
+    def __init__(self, rank: int, world: int, max_tokens: int, hidden: int, dtype: torch.dtype,
+                 device: torch.device, own_buf: int, rank_bufs: list[int], opened: list[int]):
+        self.rank, self.world = rank, world
+        self.max_tokens, self.hidden, self.dtype = max_tokens, hidden, dtype
+        self.device = torch.device(device)
+        self.buf = own_buf
+        self._rank_bufs = (ctypes.c_void_p * world)(*rank_bufs)
+        self._opened = opened  # peer mappings to close
+        self._owned = [own_buf]  # buffers to free
+        self._closed = False
+
+    # ------------------------------------------------------------ setup ----
+    @staticmethod
+    def buffer_bytes(world: int, max_tokens: int, hidden: int, dtype: torch.dtype) -> int:
+        n = _lib.load().ps_comm_buffer_bytes(world, max_tokens, hidden, _lib.dtype_code(dtype))
+        if n == 0:
+            raise ValueError(f"unsupported fused all-reduce buffer (world={world}, max_tokens={max_tokens}, "
+                             f"hidden={hidden}, dtype={dtype})")
+        return n
+
+    @staticmethod
+    def _alloc(nbytes: int) -> int:
+        p = ctypes.c_void_p()
+        _lib.check(_lib.load().ps_comm_alloc(ctypes.byref(p), nbytes), "comm_alloc")
+        return p.value
+
+    @classmethod
+    def create(cls, rank: int, world: int, max_tokens: int, hidden: int, dtype: torch.dtype, device,
+               group=None) -> "FusedAllReduce":
+        """Collective over ``group`` (every rank calls it): allocate, share
+        handles with all_gather_object, open the peers' buffers."""
+        import torch.distributed as dist
+        lib = _lib.load()
+        device = torch.device(device)
+        torch.cuda.set_device(device)
+        own = cls._alloc(cls.buffer_bytes(world, max_tokens, hidden, dtype))
+        h = (ctypes.c_char * HANDLE_BYTES)()
+        _lib.check(lib.ps_ipc_get_handle(own, h), "ipc_get_handle")
+        handles: list = [None] * world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        bufs, opened = [], []
+        for r, hr in enumerate(handles):
+            if r == rank:
+                bufs.append(own)
+                continue
+            p = ctypes.c_void_p()
+            hb = (ctypes.c_char * HANDLE_BYTES).from_buffer_copy(hr)
+            _lib.check(lib.ps_ipc_open_handle(hb, ctypes.byref(p)), "ipc_open_handle")
+            bufs.append(p.value)
+            opened.append(p.value)
+        dist.barrier(group=group)
+        return cls(rank, world, max_tokens, hidden, dtype, device, own, bufs, opened)
+
+    @classmethod
+    def emulated(cls, world: int, max_tokens: int, hidden: int, dtype: torch.dtype, device) -> list["FusedAllReduce"]:
+        """``world`` ranks' buffers in this process on one GPU; rank r's
+        object pushes into all of them. Issue every rank's producer before any
+        consumer of the same set (nothing then waits on a later launch)."""
+        device = torch.device(device)
+        torch.cuda.set_device(device)
+        nbytes = cls.buffer_bytes(world, max_tokens, hidden, dtype)
+        bufs = [cls._alloc(nbytes) for _ in range(world)]
+        objs = [cls(r, world, max_tokens, hidden, dtype, device, bufs[r], bufs, []) for r in range(world)]
+        objs[0]._owned = bufs  # rank 0's object frees them all
+        for o in objs[1:]:
+            o._owned = []
+        return objs
+
+    def close(self) -> None:
+        if self._closed:
+            return
+        self._closed = True
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            lib.ps_ipc_close(p)
+        for p in self._owned:
+            lib.ps_comm_free(p)
+
+    # --------------------------------------------------------- kernels ----
+    def linear_push(self, x: torch.Tensor, weight, set_: int, workspace=None) -> None:
+        """Row-parallel local product of this rank (x (M, K_shard) @ W.T), pushed
+        to every rank's slot ``set_``. ``weight``: QuantizedWeight (int8,
+        per-row scale) or a bf16/f16 tensor (N, K_shard)."""
+        from .quantization import LinearWorkspace, QuantizedWeight, _default_ws
+        _lib.require_cuda(x)
+        M, K = x.shape
+        if M > self.max_tokens:
+            raise ValueError(f"{M} tokens exceed the fused all-reduce capacity {self.max_tokens}")
+        lib = _lib.load()
+        if isinstance(weight, QuantizedWeight):
+            N = weight.q.shape[0]
+            w_ptr, wdt, wt_ptr, sc_ptr = weight.q.data_ptr(), _lib.PS_I8, weight.tiled().data_ptr(), \
+                weight.scale.data_ptr()
+        else:
+            N = weight.shape[0]
+            w_ptr, wdt, wt_ptr, sc_ptr = weight.data_ptr(), _lib.dtype_code(weight.dtype), None, None
+        if N != self.hidden:
+            raise ValueError(f"output width {N} != hidden {self.hidden}")
+        ws_bytes = lib.ps_w8a16_linear_tiled_workspace_size(M, N, K)
+        if workspace is None:
+            workspace = _default_ws.setdefault(x.device, LinearWorkspace())
+        buf = workspace.get(ws_bytes, x.device)
+        _lib.check(lib.ps_linear_push(x.data_ptr(), w_ptr, wdt, wt_ptr, sc_ptr, M, N, K, _lib.dtype_code(x.dtype),
+                                      self._rank_bufs, self.world, self.rank, set_, self.max_tokens, _lib.ptr(buf),
+                                      ws_bytes, _lib.stream_ptr(x.device)), "linear_push")
+
+    def allreduce_rmsnorm(self, x: torch.Tensor | None, weight: torch.Tensor | None, eps: float, set_: int,
+                          M: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Consume ``set_``: with ``weight``, x += sum of the ranks' slots (in
+        place) and return rmsnorm(x) * weight; without, return the sum."""
+        H = self.hidden
+        if weight is not None:
+            _lib.require_cuda(x, weight)
+            M = x.shape[0]
+        if M is None:
+            raise ValueError("M is required without a residual tensor")
+        if out is None:
+            out = torch.empty((M, H), dtype=self.dtype, device=self.device)
+        _lib.check(_lib.load().ps_allreduce_rmsnorm(out.data_ptr(), _lib.ptr(x), _lib.ptr(weight), float(eps), M, H,
+                                                     _lib.dtype_code(self.dtype), self.buf, self.world, set_,
+                                                     self.max_tokens, _lib.stream_ptr(self.device)),
+                   "allreduce_rmsnorm")
+        return out
+
+    def row_parallel_linear(self, x_shard: torch.Tensor, weight, set_: int = 0, workspace=None) -> torch.Tensor:
+        """engine/tensor_parallel.py:34-48 on this transport: the full (M, N)
+        output, identical on every rank. Every rank must call it."""
+        self.linear_push(x_shard, weight, set_, workspace)
+        return self.allreduce_rmsnorm(None, None, 0.0, set_, M=x_shard.shape[0])

@@ -92,6 +92,34 @@ int ps_w8a16_linear_tiled(void* y, const void* x, const int8_t* q_tiled, const f
 
 size_t ps_w8a16_linear_tiled_workspace_size(int M, int N, int K) { return ps_host::linear_tc_workspace(M, N, K); }
 
+int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale, int M, int N,
+                   int K, int dtype, void* const* rank_bufs, int world, int rank, int set, int max_tokens, void* ws,
+                   size_t ws_bytes, ps_stream_t stream) {
+  const bool int8 = wdtype == PS_I8;
+  if (M <= 0 || N <= 0 || K <= 0 || M > max_tokens || !x || (int8 ? (!w_tiled || !scale) : !w)) {
+    ps_host::set_error("linear_push: invalid arguments (M=%d N=%d K=%d max_tokens=%d)", M, N, K, max_tokens);
+    return PS_ERR_INVALID;
+  }
+  if ((dtype != PS_BF16 && dtype != PS_F16) || (!int8 && wdtype != dtype)) {
+    ps_host::set_error("linear_push: bf16/f16 activations with int8 or same-type weights");
+    return PS_ERR_UNSUPPORTED;
+  }
+  if (!ps_host::aligned(x, 16) || !ps_host::aligned(w, 16) || !ps_host::aligned(w_tiled, 16) ||
+      !ps_host::aligned(scale, 16) || K % 16 != 0 || N % 8 != 0) {
+    ps_host::set_error("linear_push: tensors must be 16-byte aligned, K a multiple of 16, N of 8");
+    return PS_ERR_INVALID;
+  }
+  ps::PushTargets pt;
+  const int rc = ps_host::push_targets(&pt, rank_bufs, world, rank, set, max_tokens, N, 2);
+  if (rc != PS_OK) return rc;
+  const int8_t* wt = int8 ? w_tiled : nullptr;
+  const int r2 = ps_host::linear_tc(nullptr, x, int8 ? static_cast<const void*>(w_tiled) : w, wdtype, scale, nullptr,
+                                    nullptr, M, N, K, dtype, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream),
+                                    wt, &pt);
+  if (r2 == PS_ERR_UNSUPPORTED) ps_host::set_error("linear_push: no tensor-core configuration for this shape");
+  return r2;
+}
+
 int ps_linear(void* y, const void* x, const void* w, const void* bias, const void* resid, int M, int N, int K,
               int dtype, void* ws, size_t ws_bytes, ps_stream_t stream) {
   return linear_any(y, x, w, dtype, nullptr, bias, resid, M, N, K, dtype, ws, ws_bytes, stream, "linear");

@@ -263,6 +263,7 @@ struct TcParams {
   int k_tiles;      // total K tiles of 64
   int k_tiles_per_split;
   int splits;
+  PushTargets push;  // world > 0: the final output goes to every rank's receive slot instead of y
 };
 
 // Shared-memory plan of one configuration.
@@ -527,8 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < cnt; ++j) dst[j] = o[j];
               }
             } else {
-              T* dst = y + static_cast<long long>(m) * p.N + nb;
-              const T* rs = resid ? resid + static_cast<long long>(m) * p.N + nb : nullptr;
+              const long long off = static_cast<long long>(m) * p.N + nb;
+              const T* rs = resid ? resid + off : nullptr;
+              const int ndst = p.push.world > 0 ? p.push.world : 1;
               if (cnt == 32 && (p.N % 8) == 0) {
                 if (rs) {
                   float rv[32];
@@ -537,13 +539,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                   for (int j = 0; j < 32; ++j) o[j] = to_f32(from_f32<T>(o[j])) + rv[j];
                 }
+                uint4 pk[4];
 #pragma unroll
-                for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = pack8<T>(o + j);
+                for (int j = 0; j < 4; ++j) pk[j] = pack8<T>(o + 8 * j);
+                for (int d = 0; d < ndst; ++d) {  // push: every rank's slot (peers over NVLink)
+                  T* dst = (p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off;
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = pk[j];
+                }
               } else {
-                for (int j = 0; j < cnt; ++j) {
-                  float v2 = o[j];
-                  if (rs) v2 = to_f32(from_f32<T>(v2)) + to_f32(rs[j]);
-                  dst[j] = from_f32<T>(v2);
+                for (int d = 0; d < ndst; ++d) {
+                  T* dst = (p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off;
+                  for (int j = 0; j < cnt; ++j) {
+                    float v2 = o[j];
+                    if (rs) v2 = to_f32(from_f32<T>(v2)) + to_f32(rs[j]);
+                    dst[j] = from_f32<T>(v2);
+                  }
                 }
               }
             }
@@ -560,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
   }
+  if (p.push.world > 0 && p.splits == 1) push_arrive(p.push);
 }
 
 // Split-K finish: y = scale * sum_s part[s] + bias (+ residual), 4 outputs
@@ -567,7 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T>
 __global__ void splitk_reduce_kernel(T* __restrict__ y, const float* __restrict__ part,
                                      const float* __restrict__ scale, const T* __restrict__ bias,
-                                     const T* __restrict__ resid, int M, int N, int splits) {
+                                     const T* __restrict__ resid, int M, int N, int splits,
+                                     const PushTargets push) {
   const int nq = N / 4;
   const long long total = static_cast<long long>(M) * nq;
   const long long plane = static_cast<long long>(M) * N;
@@ -601,10 +614,18 @@ __global__ void splitk_reduce_kernel(T* __restrict__ y, const float* __restrict_
       o[j] = o[j] * (scale ? scale[n + j] : 1.f) + (bias ? to_f32(bias[n + j]) : 0.f);
       if (resid) o[j] = to_f32(from_f32<T>(o[j])) + to_f32(resid[m * N + n + j]);
     }
-    T* dst = y + m * N + n;
+    T v4[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = from_f32<T>(o[j]);
+    for (int j = 0; j < 4; ++j) v4[j] = from_f32<T>(o[j]);
+    const uint2 u = *reinterpret_cast<const uint2*>(v4);
+    if (push.world > 0) {
+      for (int d = 0; d < push.world; ++d)  // every rank's slot (peers over NVLink)
+        *reinterpret_cast<uint2*>(static_cast<T*>(push.dst[d]) + m * N + n) = u;
+    } else {
+      *reinterpret_cast<uint2*>(y + m * N + n) = u;
+    }
   }
+  if (push.world > 0) push_arrive(push);
 }
 
 // Re-tile a row-major int8 weight [N][K] into 8 KB blocks [N/128][K/64][128][64]
@@ -745,7 +766,7 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, 
   if (blocks > 148 * 8) blocks = 148 * 8;
   splitk_reduce_kernel<T><<<static_cast<int>(blocks), 256, 0, s>>>(
       static_cast<T*>(p.y), p.part, p.scale, static_cast<const T*>(p.bias), static_cast<const T*>(p.resid), p.M,
-      p.N, pl.splits);
+      p.N, pl.splits, p.push);
   ps_host::count_launch();
   return ps_host::check_launch("linear_tc(split-K reduce)");
 }
@@ -802,7 +823,7 @@ int tile_int8(int8_t* dst, const int8_t* src, int N, int K, cudaStream_t s) {
 
 int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
               const void* resid, int M, int N, int K, int dtype, void* workspace, size_t workspace_bytes,
-              cudaStream_t s, const int8_t* w_tiled) {
+              cudaStream_t s, const int8_t* w_tiled, const ps::PushTargets* push) {
   if (dtype != PS_BF16 && dtype != PS_F16) return PS_ERR_UNSUPPORTED;
   const bool int8 = wdtype == PS_I8;
   if (!int8 && wdtype != dtype) return PS_ERR_UNSUPPORTED;
@@ -826,6 +847,11 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   p.k_tiles = pl.k_tiles;
   p.k_tiles_per_split = pl.per_split;
   p.splits = pl.splits;
+  if (push) {
+    // the push path writes whole 16-byte (epilogue) / 8-byte (split-K) groups
+    if (resid || bias || N % 8 != 0) return PS_ERR_UNSUPPORTED;
+    p.push = *push;
+  }
   if (pl.splits > 1) {
     const size_t need = ws_bytes(pl, M, N);
     if (!workspace || workspace_bytes < need) {

@@ -162,11 +162,15 @@ class PagedCausalLM:
 
     @classmethod
     def from_state_dict(cls, state_dict: dict, shape, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
-                        quantize: bool = True, max_position: int | None = None, tp=None) -> "PagedCausalLM":
+                        quantize: bool = True, max_position: int | None = None, tp=None, tp_comm: str = "fused",
+                        tp_max_tokens: int = 4096) -> "PagedCausalLM":
         """Build from an HF-named state dict (numpy or torch tensors) and a
         ``synthetic.Qwen2Shape`` (the seeded random-init checkpoints). With
         ``tp`` (a ``tensor_parallel.TPGroup``) this rank loads only its
-        Megatron shard (engine/tensor_parallel.py)."""
+        Megatron shard (engine/tensor_parallel.py). ``tp_comm`` picks the
+        row-parallel reduction: "fused" (peer-memory push from the linear into
+        the next RMSNorm, at most ``tp_max_tokens`` tokens per step) or "nccl"
+        (torch.distributed all_reduce, the reference's collective)."""
         cfg = SimpleNamespace(num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
                               hidden_size=shape.hidden, head_dim=shape.head_dim, rms_norm_eps=shape.rms_eps,
                               rope_theta=shape.rope_theta, rope_parameters=None,
@@ -174,10 +178,10 @@ class PagedCausalLM:
                               num_hidden_layers=shape.num_layers, vocab_size=shape.vocab,
                               intermediate_size=shape.intermediate, tie_word_embeddings=shape.tie_embeddings)
         obj = cls.__new__(cls)
-        obj._init(cfg, state_dict, device, dtype, quantize, shape.rope_theta, tp)
+        obj._init(cfg, state_dict, device, dtype, quantize, shape.rope_theta, tp, tp_comm, tp_max_tokens)
         return obj
 
-    def _init(self, config, sd, device, dtype, quantize, theta, tp=None):
+    def _init(self, config, sd, device, dtype, quantize, theta, tp=None, tp_comm="fused", tp_max_tokens=4096):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback)")
@@ -312,6 +316,13 @@ class PagedCausalLM:
                                                             self.device)
         self.attn_ws = AttentionWorkspace()
         self.lin_ws = LinearWorkspace()
+        if tp_comm not in ("fused", "nccl"):
+            raise ValueError(f"tp_comm must be 'fused' or 'nccl', not {tp_comm!r}")
+        self.comm = None
+        if self.tp is not None and tp_comm == "fused":
+            from .comm import FusedAllReduce
+            self.comm = FusedAllReduce.create(self.tp.rank, self.tp.world, tp_max_tokens, self.hidden_size, dtype,
+                                              self.device, self.tp.group)
         self.k_cache = None
         self.v_cache = None
         self.block_size = None
@@ -362,8 +373,15 @@ class PagedCausalLM:
         q = torch.empty((T, hq, d), dtype=self.dtype, device=self.device)
         attn = torch.empty((T, hq, d), dtype=self.dtype, device=self.device)
         num_slots = self.num_blocks * self.block_size
+        comm = self.comm  # fused TP reduction: o_proj -> set 0, down_proj -> set 1, consumed by the next norm
+        if comm is not None and T > comm.max_tokens:
+            raise ValueError(f"{T} tokens exceed tp_max_tokens={comm.max_tokens}")
+        pending = False  # a down_proj reduction waits in set 1
         for li, fl in enumerate(self.fused):
-            h = rms_norm_fused(x, fl.input_ln, self.rms_eps)
+            if pending:
+                h = comm.allreduce_rmsnorm(x, fl.input_ln, self.rms_eps, 1)
+            else:
+                h = rms_norm_fused(x, fl.input_ln, self.rms_eps)
             qkv = self._linear(h, fl.qkv, fl.qkv_b)
             kc, vc = self.k_cache[li], self.v_cache[li]
             _lib.check(lib.ps_rope_qkv_write_kv(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), qkv.data_ptr(),
@@ -373,21 +391,41 @@ class PagedCausalLM:
             for (s, e, _) in runs:
                 paged_attention(q, kc, vc, meta.block_tables[s:e], meta.cu_q[s:e + 1], meta.start_pos[s:e],
                                 max(meta.q_lens[s:e]), max(meta.ctx_lens[s:e]), out=attn, workspace=self.attn_ws)
-            x = self._linear(attn.view(T, hq * d), fl.o, residual=x if lead else None)
-            if self.tp is not None:
-                self.tp.all_reduce_(x)
-            h = rms_norm_fused(x, fl.post_ln, self.rms_eps)
+            if comm is not None:
+                comm.linear_push(attn.view(T, hq * d), fl.o, 0, workspace=self.lin_ws)
+                h = comm.allreduce_rmsnorm(x, fl.post_ln, self.rms_eps, 0)
+            else:
+                x = self._linear(attn.view(T, hq * d), fl.o, residual=x if lead else None)
+                if self.tp is not None:
+                    self.tp.all_reduce_(x)
+                h = rms_norm_fused(x, fl.post_ln, self.rms_eps)
             gu = self._linear(h, fl.gate_up)
             act = torch.empty((T, self.intermediate_size), dtype=self.dtype, device=self.device)
             _lib.check(lib.ps_silu_mul(act.data_ptr(), gu.data_ptr(), T, self.intermediate_size,
                                        _lib.dtype_code(self.dtype), stream), "silu_mul")
-            x = self._linear(act, fl.down, residual=x if lead else None)
-            if self.tp is not None:
-                self.tp.all_reduce_(x)
-        if logits_rows is not None:
-            x = x.index_select(0, logits_rows)
-        x = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
+            if comm is not None:
+                comm.linear_push(act, fl.down, 1, workspace=self.lin_ws)
+                pending = True
+            else:
+                x = self._linear(act, fl.down, residual=x if lead else None)
+                if self.tp is not None:
+                    self.tp.all_reduce_(x)
+        if pending:  # the last down_proj reduction, consumed by the final norm (all rows, then the selection)
+            x = comm.allreduce_rmsnorm(x, self.final_norm_w, self.rms_eps, 1)
+            if logits_rows is not None:
+                x = x.index_select(0, logits_rows)
+        else:
+            if logits_rows is not None:
+                x = x.index_select(0, logits_rows)
+            x = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
         return linear16(x, self.lm_head_w, workspace=self.lin_ws)
+
+    def close(self) -> None:
+        """Release the fused all-reduce buffers and peer mappings (call on
+        every rank before destroy_process_group)."""
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     def forward_step(self, input_ids: torch.Tensor, block_table: list[int], start_pos: int) -> torch.Tensor:
         """engine/model.py:149-193: one chunk of one sequence; returns

@@ -46,7 +46,8 @@ def test_library_metadata_calls_without_gpu():
     assert isinstance(lib.ps_launch_count(), int)
     # size queries are pure host arithmetic
     assert lib.ps_paged_attention_workspace_size(64, 1, 4096, 16, 2, 128) > 0
-    assert lib.ps_paged_attention_workspace_size(1, 512, 512, 16, 2, 128) == 0
+    # a prefill chunk shorter than two key tiles runs unsplit: no scratch
+    assert lib.ps_paged_attention_workspace_size(1, 64, 64, 16, 2, 128) == 0
 
 
 def test_host_validation_errors_without_gpu():

@@ -1,0 +1,152 @@
+"""The fused tensor-parallel all-reduce kernels (ps_linear_push +
+ps_allreduce_rmsnorm) on one GPU, with W ranks emulated in one process:
+every rank's push is issued before any rank's consume of the same set, so
+no kernel waits for a later launch. Checked against the unfused path:
+per-rank partials from the plain W8A16/16-bit linear (engine/
+tensor_parallel.py:34-46), summed in rank order (the all-reduce,
+tensor_parallel.py:47), then the residual add and RMSNorm of
+engine/model.py:184-190."""
+
+import pytest
+import torch
+
+from pageserve_b200 import _lib
+from pageserve_b200.comm import FusedAllReduce
+from pageserve_b200.model import rms_norm_fused
+from pageserve_b200.quantization import QuantizedWeight, linear16
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 2e-2  # bf16 output of a different reduction order (the RMSNorm)
+
+
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def rel_err(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def _partial(x, w):
+    if isinstance(w, QuantizedWeight):
+        return w.linear(x)
+    return linear16(x, w)
+
+
+def _weights(world, N, K, int8, dev, g):
+    ws = []
+    for _ in range(world):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        ws.append(QuantizedWeight(w) if int8 else w)
+    return ws
+
+
+@pytest.mark.parametrize("world,M,N,K,int8", [
+    (2, 576, 2048, 1024, True),    # TP2 o_proj of the 3B shape, prefill+decode batch (split-K writer)
+    (2, 64, 2048, 5504, True),     # TP2 down_proj, decode batch
+    (4, 96, 1024, 256, True),      # 4 K tiles: no split, the GEMM epilogue pushes
+    (2, 40, 512, 640, False),      # 16-bit weight (SS operands)
+    (1, 33, 256, 512, True),       # degenerate world of one
+    (8, 17, 2048, 256, True),      # TP8 o_proj width
+])
+def test_push_then_allreduce_rmsnorm(world, M, N, K, int8):
+    _need_gpu()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(world * 1000 + M)
+    ranks = FusedAllReduce.emulated(world, max_tokens=max(M, 64), hidden=N, dtype=torch.bfloat16, device=dev)
+    try:
+        xs = [torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16) for _ in range(world)]
+        ws = _weights(world, N, K, int8, dev, g)
+        norm_w = (1 + 0.1 * torch.randn(N, device=dev, generator=g)).to(torch.bfloat16)
+        resid = [torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16) for _ in range(world)]
+        resid = [resid[0].clone() for _ in range(world)]  # every rank holds the same residual stream
+        partials = [_partial(xs[r], ws[r]) for r in range(world)]
+        s = torch.zeros(M, N, dtype=torch.float32, device=dev)
+        for p in partials:
+            s += p.float()
+        s = s.to(torch.bfloat16)
+        x_ref = (resid[0].float() + s.float()).to(torch.bfloat16)
+        y_ref = rms_norm_fused(x_ref, norm_w, 1e-6)
+        # three rounds over both sets: the flags re-arm
+        for it in range(3):
+            for set_ in (0, 1):
+                for r in range(world):
+                    ranks[r].linear_push(xs[r], ws[r], set_)
+                if set_ == 0:
+                    xr = [resid[r].clone() for r in range(world)]
+                    ys = [ranks[r].allreduce_rmsnorm(xr[r], norm_w, 1e-6, set_) for r in range(world)]
+                    torch.cuda.synchronize()
+                    for r in range(world):
+                        assert torch.equal(xr[r], x_ref), f"round {it} rank {r}: residual stream"
+                        assert torch.equal(ys[r], ys[0]), f"round {it}: ranks disagree"
+                    assert rel_err(ys[0].float(), y_ref.float()) < REL_TOL
+                else:
+                    outs = [ranks[r].allreduce_rmsnorm(None, None, 0.0, set_, M=M) for r in range(world)]
+                    torch.cuda.synchronize()
+                    for r in range(world):
+                        assert torch.equal(outs[r], s), f"round {it} rank {r}: plain all-reduce"
+        _lib.raise_on_device_error()
+    finally:
+        ranks[0].close()
+
+
+def test_row_parallel_linear_on_push_transport_matches_oracle():
+    """tensor_parallel.py:34-48 semantics (the sum of the ranks' partials of
+    a column-split weight) against the numpy oracle."""
+    _need_gpu()
+    from oracle import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    world, M, N, K = 2, 48, 768, 1024
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    q, sc = ops.quantize_per_channel(w.float().cpu().numpy())
+    xn = x.float().cpu().numpy()
+    shards = [slice(r * K // world, (r + 1) * K // world) for r in range(world)]
+    ref = ops.round_bf16(sum(ops.round_bf16(ops.quantized_linear(xn[:, sl], q[:, sl], sc)) for sl in shards))
+    full = QuantizedWeight(w)
+    ranks = FusedAllReduce.emulated(world, max_tokens=M, hidden=N, dtype=torch.bfloat16, device=dev)
+    try:
+        shards = []
+        for r in range(world):
+            sl = slice(r * K // world, (r + 1) * K // world)
+            shards.append(QuantizedWeight.from_quantized(full.q[:, sl].contiguous(), full.scale, torch.bfloat16))
+        for r in range(world):
+            ranks[r].linear_push(x[:, r * K // world:(r + 1) * K // world].contiguous(), shards[r], 0)
+        outs = [ranks[r].allreduce_rmsnorm(None, None, 0.0, 0, M=M) for r in range(world)]
+        torch.cuda.synchronize()
+        assert torch.equal(outs[0], outs[1])
+        assert rel_err(outs[0].float().cpu(), torch.from_numpy(ref).float()) < REL_TOL
+    finally:
+        ranks[0].close()
+
+
+def test_consumer_wait_times_out_without_producer():
+    """A flag that nothing raises: the bounded wait gives up (a few
+    seconds), records the timeout in the device status word, and the
+    context stays usable."""
+    _need_gpu()
+    dev = torch.device("cuda", 0)
+    (rank,) = FusedAllReduce.emulated(1, max_tokens=8, hidden=256, dtype=torch.bfloat16, device=dev)
+    try:
+        _lib.raise_on_device_error()  # nothing pending from earlier tests
+        x = torch.zeros(4, 256, dtype=torch.bfloat16, device=dev)
+        w = torch.ones(256, dtype=torch.bfloat16, device=dev)
+        rank.allreduce_rmsnorm(x, w, 1e-6, 1)
+        torch.cuda.synchronize()
+        assert _lib.device_status(clear=True) == 4  # kErrTimeout
+        # still usable: a normal push/consume round afterwards
+        xin = torch.randn(4, 64, device=dev).to(torch.bfloat16)
+        wt = (torch.randn(256, 64, device=dev) * 0.1).to(torch.bfloat16)
+        rank.linear_push(xin, wt, 1)
+        out = rank.allreduce_rmsnorm(None, None, 0.0, 1, M=4)
+        torch.cuda.synchronize()
+        assert torch.equal(out, linear16(xin, wt))
+        _lib.raise_on_device_error()
+    finally:
+        rank.close()

@@ -1,5 +1,7 @@
-"""Tensor parallelism on 2 GPUs (NCCL): a TP=2 sharded model produces the
-TP=1 model's logits and greedy tokens. Skipped with fewer than 2 GPUs."""
+"""Tensor parallelism on 2 GPUs: a TP=2 sharded model produces the TP=1
+model's logits and greedy tokens, with the row-parallel reductions either
+fused (peer-memory push into the next RMSNorm) or on NCCL all_reduce.
+Skipped with fewer than 2 GPUs. NVLS stays off (plain peer memory only)."""
 
 import os
 import tempfile
@@ -12,21 +14,22 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _tp_worker(rank, world, port, out_file):
+def _tp_worker(rank, world, port, out_file, tp_comm):
     import datetime
 
     import torch.distributed as dist
 
-    from pageserve_b200 import synthetic
+    from pageserve_b200 import _lib, synthetic
     from pageserve_b200.model import PagedCausalLM
     from pageserve_b200.tensor_parallel import TPGroup
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     shape = synthetic.TINY
     sd = synthetic.generate_state_dict(shape, seed=9, perturb_norms_biases=True)
-    m = PagedCausalLM.from_state_dict(sd, shape, device=f"cuda:{rank}", quantize=True, tp=TPGroup(rank, world))
+    m = PagedCausalLM.from_state_dict(sd, shape, device=f"cuda:{rank}", quantize=True, tp=TPGroup(rank, world),
+                                      tp_comm=tp_comm, tp_max_tokens=64)
     m.allocate_kv_cache(40, 4)
     rng = np.random.default_rng(4)
     prompts = [rng.integers(0, shape.vocab, size=n) for n in (11, 23)]
@@ -41,15 +44,18 @@ def _tp_worker(rank, world, port, out_file):
         r1, rt = ref.forward_batch(np.concatenate([prompts[1][:20], [7]]), [20, 1], [0, 11], [tables[1], tables[0]])
         res.update(ref0=r0.float().cpu(), ref1=r1.float().cpu(), reftok=rt.cpu())
     torch.save(res, f"{out_file}.{rank}")
+    _lib.raise_on_device_error()
+    m.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_tp2_matches_tp1():
+@pytest.mark.parametrize("tp_comm,port", [("fused", 29517), ("nccl", 29519)])
+def test_tp2_matches_tp1(tp_comm, port):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_tp_worker, args=(2, 29517, os.path.join(tmp, "r")), nprocs=2, join=True)
+        mp.spawn(_tp_worker, args=(2, port, os.path.join(tmp, "r"), tp_comm), nprocs=2, join=True)
         a = torch.load(os.path.join(tmp, "r.0"), weights_only=True)
         b = torch.load(os.path.join(tmp, "r.1"), weights_only=True)
     for k in ("lg0", "lg1", "tok"):
