@@ -118,7 +118,7 @@ class Clocks:
 
 # ------------------------------------------------------------- workload ----
 
-def build_workload(device, seed=0, tp=None):
+def build_workload(device, seed=0, tp=None, tp_comm="fused"):
     import numpy as np
     import torch
 
@@ -128,7 +128,7 @@ def build_workload(device, seed=0, tp=None):
     shape = synthetic.QWEN25_3B
     sd = synthetic.TorchStateDict(shape, seed=seed, device=device)
     m = PagedCausalLM.from_state_dict(sd, shape, device=device, dtype=torch.bfloat16, quantize=True,
-                                      max_position=4096, tp=tp)
+                                      max_position=4096, tp=tp, tp_comm=tp_comm, tp_max_tokens=N_DECODE + PREFILL)
     del sd
     torch.cuda.empty_cache()
     nblk_dec = CTX // BLOCK
@@ -152,23 +152,33 @@ def build_workload(device, seed=0, tp=None):
     return m, dict(q_lens=q_lens, start_pos=start_pos, tables=tables, ids=ids, shape=shape)
 
 
-def time_events(fn, iters, stream=None):
+def time_events(fn, iters):
+    """Device time of one ``fn`` call (ms): ``iters`` calls captured once into
+    a CUDA graph, the graph replayed between CUDA events on the current
+    stream (the way the step runs them, without host launch gaps)."""
     import torch
 
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    g.replay()
+    end.record()
     torch.cuda.synchronize()
-    start.record(stream)
-    for _ in range(iters):
-        fn()
-    end.record(stream)
-    torch.cuda.synchronize()
-    return start.elapsed_time(end) / iters  # ms
+    ms = start.elapsed_time(end) / iters
+    del g
+    return ms
 
 
 def kernel_breakdown(m, w, peaks):
-    """Each main kernel of the step timed alone with CUDA events, rotating
-    over the 36 layers' weights / caches so nothing is served from L2."""
+    """Each main kernel of the step timed alone (CUDA-graph replay between
+    CUDA events), rotating over the 36 layers' weights / caches so nothing
+    is served from L2."""
     import torch
 
     from pageserve_b200.paged_attention import AttentionWorkspace, paged_attention
@@ -191,7 +201,7 @@ def kernel_breakdown(m, w, peaks):
         def f():
             wgt = get_w(m.fused[ctr[0] % L])
             ctr[0] += 1
-            outs["y"] = w8a16_linear(x, wgt.q, wgt.scale, workspace=ws)
+            outs["y"] = w8a16_linear(x, wgt.q, wgt.scale, workspace=ws, q_tiled=wgt.tiled())
         f()
         ms = time_events(f, 2 * L)
         wgt = get_w(m.fused[0])
@@ -313,7 +323,7 @@ def run_gpu(args):
 
     peaks = _peaks()
     tp = TPGroup.from_default() if (world > 1 and not args.replicas) else None
-    m, w = build_workload(device, seed=0 if tp else rank, tp=tp)
+    m, w = build_workload(device, seed=0 if tp else rank, tp=tp, tp_comm=args.tp_comm)
     max_blocks = max(len(t) for t in w["tables"])
     g = StepGraph(m, w["q_lens"], max_blocks, CTX, w["start_pos"], w["tables"], w["ids"])
     for _ in range(args.warmup):
@@ -361,16 +371,12 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
     if rank != 0:
-        del g
-        if world > 1:
-            dist.destroy_process_group()
+        _finish(g, m, world)
         return
     if kb is None:
         print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "ms_per_step": ms / args.steps,
                           "note": "profiling run (no breakdown)"}), flush=True)
-        del g
-        if world > 1:
-            dist.destroy_process_group()
+        _finish(g, m, world)
         return
     # dominant kernel: the largest per-step time share among the measured classes
     per_step = {k: v["ms"] * (36 if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode") else 1)
@@ -394,7 +400,9 @@ def run_gpu(args):
             "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random init, random KV contents)",
             "config": _config({"parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
-                               else "single GPU"}),
+                               else "single GPU",
+                               **({"tp_allreduce": "fused peer-memory push (o_proj/down -> next RMSNorm)"
+                                   if args.tp_comm == "fused" else "NCCL all_reduce"} if tp else {})}),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": g.h2d_bytes, "d2h_bytes_per_step": g.d2h_bytes,
                     "api": "StepGraph.run (host ids/metadata in, host next tokens out)"},
             "gpu_launches": launches, "launches_per_step": g.launches_per_replay,
@@ -404,8 +412,17 @@ def run_gpu(args):
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "clocks": clocks}
     print(json.dumps(line), flush=True)
-    del g
+    _finish(g, m, world)
+
+
+def _finish(g, m, world):
+    """Release the CUDA graph (it may hold NCCL calls) and the fused
+    all-reduce's IPC mappings on every rank, then leave the process group."""
+    import torch.distributed as dist
+    g.release()
+    m.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -418,6 +435,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-breakdown", action="store_true", help="skip the per-kernel timing (for profiling runs)")
     ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
+    ap.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
+                    help="N>1 tensor parallelism: row-parallel reduction transport")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -220,6 +220,8 @@ PS_API int ps_argmax(int32_t* out_dev, const void* logits_dev, int M, int V, int
  *   bytes [0, PS_COMM_CTRL_BYTES): u32 control words; set s in {0, 1} has its
  *     arrival flag at 4*s (written by every rank's producer), its consumed
  *     counter at 64 + 4*s and its producer CTA counter at 128 + 4*s (local);
+ *     a 'broken' word at 192, set by the first wait that times out, makes
+ *     every later wait on this buffer give up at once (re-zero to clear);
  *   then slots [2 sets][world][max_tokens][hidden] of dtype.
  * The two sets alternate (o_proj -> set 0, down_proj -> set 1). Every wait is
  * bounded (a few seconds); on timeout PS_ERR_TIMEOUT-style code 4 is recorded
@@ -231,6 +233,9 @@ PS_API size_t ps_comm_buffer_bytes(int world, int max_tokens, int hidden, int dt
 /* cudaMalloc + zero fill (IPC-shareable device memory). */
 PS_API int ps_comm_alloc(void** buf_dev, size_t bytes);
 PS_API int ps_comm_free(void* buf_dev);
+/* Zero this rank's control words (after a timeout; every rank resets before
+ * the next step). Synchronises `stream`. */
+PS_API int ps_comm_reset(void* buf_dev, ps_stream_t stream);
 /* cudaIpcGetMemHandle / cudaIpcOpenMemHandle on 64-byte opaque handles. */
 PS_API int ps_ipc_get_handle(void* buf_dev, void* handle64_out);
 PS_API int ps_ipc_open_handle(const void* handle64, void** peer_buf_out);

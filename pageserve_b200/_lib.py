@@ -57,6 +57,7 @@ _SIGNATURES = {
     "ps_comm_buffer_bytes": (c_size_t, [_I, _I, _I, _I]),
     "ps_comm_alloc": (c_int, [_P, c_size_t]),
     "ps_comm_free": (c_int, [_P]),
+    "ps_comm_reset": (c_int, [_P, _P]),
     "ps_ipc_get_handle": (c_int, [_P, _P]),
     "ps_ipc_open_handle": (c_int, [_P, _P]),
     "ps_ipc_close": (c_int, [_P]),

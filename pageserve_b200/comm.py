@@ -102,6 +102,11 @@ class FusedAllReduce:
             o._owned = []
         return objs
 
+    def reset(self) -> None:
+        """Re-zero this rank's control words (flags, counters, the broken
+        mark) after a timeout; every rank must reset before the next step."""
+        _lib.check(_lib.load().ps_comm_reset(self.buf, _lib.stream_ptr(self.device)), "comm_reset")
+
     def close(self) -> None:
         if self._closed:
             return

@@ -39,6 +39,10 @@ PS_DEVICE unsigned ld_acquire_sys(const unsigned* p) {
 
 PS_DEVICE unsigned* ctrl_flag(void* buf, int set) { return reinterpret_cast<unsigned*>(buf) + set; }
 PS_DEVICE unsigned* ctrl_consumed(void* buf, int set) { return reinterpret_cast<unsigned*>(buf) + 16 + set; }
+// Set by the first wait that times out: later waits on this buffer return at
+// once, so a lost peer costs one timeout, not one per layer. Cleared only by
+// re-zeroing the buffer.
+PS_DEVICE volatile unsigned* ctrl_broken(void* buf) { return reinterpret_cast<volatile unsigned*>(buf) + 48; }
 
 // One CTA per token row. NORM: x += s (in place), y = rmsnorm(x) * w;
 // otherwise y = s. s = T(sum over ranks, float32, rank order) — the same on
@@ -53,8 +57,14 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(T* __restrict__ 
   unsigned* flag = ctrl_flag(buf, set);
   if (threadIdx.x == 0) {
     const long long t0 = clock64();
+    volatile unsigned* broken = ctrl_broken(buf);
     while (ld_acquire_sys(flag) < static_cast<unsigned>(W)) {
+      if (*broken) {
+        record_error(status, kErrTimeout);
+        break;
+      }
       if (clock64() - t0 > kCommWaitCycles) {
+        *broken = 1u;
         record_error(status, kErrTimeout);
         break;
       }
@@ -160,6 +170,7 @@ int push_targets(ps::PushTargets* pt, void* const* rank_bufs, int world, int ran
     pt->flag[r] = reinterpret_cast<unsigned*>(b) + set;
   }
   pt->arrivals = reinterpret_cast<unsigned*>(rank_bufs[rank]) + 32 + set;
+  pt->max_tokens = max_tokens;
   return PS_OK;
 }
 
@@ -184,6 +195,21 @@ PS_API int ps_comm_alloc(void** buf, size_t bytes) {
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     ps_host::set_error("comm_alloc: %s", cudaGetErrorString(e));
+    return PS_ERR_CUDA;
+  }
+  return PS_OK;
+}
+
+PS_API int ps_comm_reset(void* buf, ps_stream_t stream) {
+  if (!buf) {
+    ps_host::set_error("comm_reset: null buffer");
+    return PS_ERR_INVALID;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(buf, 0, PS_COMM_CTRL_BYTES, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    ps_host::set_error("comm_reset: %s", cudaGetErrorString(e));
     return PS_ERR_CUDA;
   }
   return PS_OK;

@@ -14,6 +14,7 @@ struct PushTargets {
   void* dst[kMaxWorld];       // rank r's slot for this rank's partial, [max_tokens][N], row stride N
   unsigned* flag[kMaxWorld];  // rank r's arrival flag of this set
   unsigned* arrivals;         // this rank's CTA arrival counter of this set
+  int max_tokens;             // rows of each slot
 };
 
 PS_DEVICE void red_release_sys_add(unsigned* p, unsigned v) {
@@ -21,14 +22,15 @@ PS_DEVICE void red_release_sys_add(unsigned* p, unsigned v) {
 }
 
 // Every thread of every CTA of the writing grid calls this once, after its
-// last store. Each thread fences its own peer stores at system scope; the
-// last CTA to arrive re-arms the local counter and adds one to every rank's
-// flag, so a rank's flag reaches `world` once all ranks' outputs are in its
-// slots.
+// last store. The CTA barrier orders all its threads' stores before thread
+// 0's system-scope fence (the fence is cumulative over what the barrier made
+// visible to thread 0), whose counter increment publishes them; the last CTA
+// to arrive re-arms the local counter and adds one to every rank's flag, so
+// a rank's flag reaches `world` once all ranks' outputs are in its slots.
 PS_DEVICE void push_arrive(const PushTargets& pt) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned total = gridDim.x * gridDim.y * gridDim.z;
     const unsigned prev = atomicAdd(pt.arrivals, 1u);
     if (prev == total - 1) {

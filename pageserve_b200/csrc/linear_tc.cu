@@ -23,19 +23,22 @@
 //               weight row per lane, K packed two bf16 per column), running up
 //               to two k-tiles ahead of the MMA, which reads A from TMEM
 //               (tcgen05.mma ... [a_tmem]) and only the activations from
-//               shared memory; then the epilogue from TMEM (tcgen05.ld 32x32b;
-//               warp w reads lane quarter w%4, half of the columns),
-//               transposed through shared memory so each lane stores 16
-//               consecutive outputs (scale, bias, residual)
+//               shared memory; then they copy the accumulators from TMEM
+//               (tcgen05.ld 32x32b; warp w reads lane quarter w%4) into a
+//               token-major fp32 stage in shared memory
+//   all warps   epilogue from the stage: 8 consecutive outputs per thread
+//               (scale, bias, residual), 16-byte stores along output rows
 // The weight stream runs ahead independently of the MMA, so HBM latency is
 // hidden by the weight ring depth rather than by the MMA's commit chain.
 // Keeping the widened weights in TMEM takes their write and the MMA's read
 // (64 KB per k-tile at 256 rows) off shared memory, whose bandwidth bounds
 // this loop. bf16/f16 weights (the lm_head) skip the widening: TMA lands
 // them in shared memory as the MMA's A operand directly.
-// Small-N shapes split K across CTAs: each split stores float32 partials
-// (no atomics) and a separate wide kernel reduces them and applies the
-// epilogue (a single CTA reducing a whole tile was latency bound).
+// Small-N shapes split K across CTAs: the splits of one output tile form a
+// thread-block cluster along z, and after the main loop each CTA reduces one
+// slice of the tile's token rows over all the splits' stages through
+// distributed shared memory (ld.shared::cluster, fixed split order), so the
+// partial sums never leave the chip and no second kernel runs.
 //
 // Every mbarrier wait is bounded (about a second of clock64 cycles): on
 // timeout the kernel records kErrTimeout in the status word, stops issuing
@@ -44,6 +47,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "linear.cuh"
@@ -132,6 +136,43 @@ PS_DEVICE void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t
 }
 
 PS_DEVICE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Tiled TMA store of a shared-memory box to global (bulk async-group).
+PS_DEVICE void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+PS_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+PS_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+PS_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Shared memory of this CTA -> shared memory of a cluster peer (dst and its
+// mbarrier are cluster addresses from mapa), completing bytes on that barrier.
+PS_DEVICE void bulk_s2s(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// Barrier 1 among the 8 epilogue warps (warps 3..10).
+PS_DEVICE void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Thread-block cluster helpers (split-K CTAs of one output tile form a cluster).
+PS_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+PS_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address `addr` of this CTA -> the same offset in CTA `rank`.
+PS_DEVICE uint32_t mapa_shared(uint32_t addr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
 PS_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PS_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -257,13 +298,20 @@ struct TcParams {
   const float* scale;
   const void* bias;
   const void* resid;
-  float* part;      // split-K float32 partials [splits][M][N]
   int* status;
   int M, N, K;
   int k_tiles;      // total K tiles of 64
   int k_tiles_per_split;
-  int splits;
+  int splits;       // split-K CTAs per output tile = cluster size along z (1: no cluster)
+  int tma_out;      // splits == 1 and N % 8 == 0: outputs leave by TMA stores (OutMaps)
   PushTargets push;  // world > 0: the final output goes to every rank's receive slot instead of y
+};
+
+// Tensor maps of the TMA-stored outputs (bf16/f16 [rows][N], box 128 x BM).
+struct OutMaps {
+  CUtensorMap y;                // output [M][N]
+  CUtensorMap res;              // residual [M][N]
+  CUtensorMap dst[kMaxWorld];   // push: every rank's slot [max_tokens][N]
 };
 
 // Shared-memory plan of one configuration.
@@ -276,24 +324,26 @@ struct Cfg {
   static constexpr int kAS = 0;
   static constexpr int kAccCols = NSUB * BM;                       // fp32 accumulators
   static constexpr int kACols = kInt8 ? NSUB * (kBK / 2) : 0;      // one TMEM A stage (2 bf16 per column)
-  static constexpr int kEpi = kDeqWarps * 32 * 33 * 4;           // per-warp padded 32x32 transpose tiles
+  static constexpr int kStage = BM * 128 * 4;                     // epilogue fp32 stage [BM][128]
   static constexpr int kRX0 = (96 * 1024) / kX;
   static constexpr int kRX = kRX0 < 2 ? 2 : (kRX0 > 8 ? 8 : kRX0);
   static constexpr int kRW0 = (kSmemBudget - kAS * kA - kRX * kX) / kW;
   static constexpr int kRW = kRW0 < 2 ? 2 : (kRW0 > 8 ? 8 : kRW0);
   // layout (1024-aligned rings first): A | W | X | barriers. The epilogue's
-  // transpose tiles reuse the weight ring, idle once the main loop is done.
+  // stage reuses the rings, idle once the main loop is done.
   static constexpr int kOffA = 0;
   static constexpr int kOffW = kOffA + kAS * kA;
   static constexpr int kOffX = kOffW + kRW * kW;
-  static constexpr int kOffEpi = kOffW;
+  static constexpr int kOffStage = kOffW;
   static constexpr int kOffBar = kOffX + kRX * kX;
   static constexpr int kBytes = kOffBar + 512 + 1024;
   static constexpr int kTmemNeed = kAccCols + 2 * kACols;  // accumulators + two A stages
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 :
                                    (kTmemNeed <= 256 ? 256 : 512)));
   static_assert(kBytes <= 227 * 1024, "shared memory plan too large");
-  static_assert(kRW * kW >= kEpi, "epilogue tiles alias the weight ring");
+  static constexpr int kRings = kRW * kW + kRX * kX;
+  static_assert(kRings >= kStage, "epilogue stage aliases the rings");
+  static_assert(kRings >= NSUB * BM * 256, "TMA output tiles alias the rings");
   static_assert(kTmemNeed <= 512, "TMEM columns");
   static_assert(kW % 1024 == 0 && kX % 1024 == 0 && kA % 1024 == 0, "1024-byte aligned stages");
 };
@@ -301,7 +351,7 @@ struct Cfg {
 template <typename T, bool kInt8, int NSUB, int BM>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                     const TcParams p) {
+                     const TcParams p, const __grid_constant__ OutMaps om) {
   using C = Cfg<kInt8, NSUB, BM>;
   constexpr int RW = C::kRW, RX = C::kRX;
   extern __shared__ unsigned char smem_raw[];
@@ -319,6 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto a_full = [&](int s) { return bars + 8 * (32 + s); };
   auto a_empty = [&](int s) { return bars + 8 * (34 + s); };
   const uint32_t acc_full = bars + 8 * 36;
+  const uint32_t res_full = bars + 8 * 37;   // residual tiles landed (TMA output path)
+  const uint32_t recv_full = bars + 8 * 38;  // split-K slices from the cluster peers landed
   unsigned char* misc = gbase + C::kOffBar + 8 * 40;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 4);
@@ -347,6 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(a_empty(s), 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(res_full, 1);
+    mbar_init(recv_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -479,87 +533,186 @@ __global__ void __launch_bounds__(kThreads, 1)
         PS_TC_TRACE(16 + (i & 255) * 8 + 3, t == 0);
       }
     }
-    // ------------------------------------------------------------ epilogue --
-    // Lane = weight row n (its TMEM lane): scale and bias are per-lane
-    // scalars applied in that layout; 32 token columns at a time go through a
-    // padded shared-memory transpose so each lane then owns one token row and
-    // stores 32 consecutive outputs (64 bytes) with 16-byte stores.
-    const bool ok = nkt > 0 && warp_wait(acc_full, 0, abort_flag, p.status);
-    tc_fence_after();
-    PS_TC_TRACE(2, t == 0);
-    // acc_full implies every k-tile's MMA (and so every widening pass) is
-    // done and no weight load is in flight: the weight ring is free for the
-    // transpose tiles.
-    const int q = warp & 3;             // TMEM lane quarter this warp may read
-    const int h = (warp - 3) >> 2;      // which 32-column chunks (alternating)
-    float* tp = reinterpret_cast<float*>(gbase + C::kOffEpi) + (warp - 3) * (32 * 33);
+  }
+  // -------------------------------------------------------------- epilogue --
+  // Every warp of every CTA of the cluster takes the same barriers here; the
+  // rings are idle once acc_full fired, so the epilogue's buffers alias them.
+  //  * splits == 1, N % 8 == 0: per 128-row sub-tile the epilogue warps read
+  //    the accumulators from TMEM (lane = weight row n, 32 tokens at a time),
+  //    apply scale / bias / residual (the residual tile arrives by TMA into
+  //    the output tile first), write dtype values into a token-major
+  //    [BM][128] tile and one thread TMA-stores it (to y, or to every rank's
+  //    slot when pushing).
+  //  * splits > 1: the splits of a tile form a cluster. Each stages its fp32
+  //    accumulators ([BM][128] per sub-tile), then bulk-copies token-row
+  //    slice j to cluster CTA j, which sums the S slices in split order from
+  //    its own shared memory and stores 8 outputs per thread.
+  //  * splits == 1, N % 8 != 0: per-lane scalar stores (ragged widths).
+  {
+    bool ok = true;
+    if (warp >= 3) {
+      ok = nkt > 0 && warp_wait(acc_full, 0, abort_flag, p.status);
+      tc_fence_after();
+    }
+    PS_TC_TRACE(2, threadIdx.x == 96);
     const T* bias = static_cast<const T*>(p.bias);
     const T* resid = static_cast<const T*>(p.resid);
     T* y = static_cast<T*>(p.y);
-    const bool part = p.splits > 1;
-    if (ok) {
+    const int S = p.splits;
+    const int q = warp & 3;              // TMEM lane quarter (epilogue warps)
+    const int h = (warp - 3) >> 2;       // alternating 32-token chunks
+    if (S == 1) {
+      const uint32_t out_sa = base + C::kOffStage;  // NSUB tiles of [BM][128] dtype
+      T* out_tile = reinterpret_cast<T*>(gbase + C::kOffStage);
+      const bool use_tma = p.tma_out != 0;
+      if (use_tma && resid && threadIdx.x == 96) {
+        mbar_expect_tx(res_full, NSUB * BM * 256);
+        for (int sub = 0; sub < NSUB; ++sub) tma_load_2d(out_sa + sub * BM * 256, &om.res, res_full, n0 + sub * 128, m0);
+      }
+      if (warp >= 3) {
+        const bool res_ok = !(use_tma && resid) || warp_wait(res_full, 0, abort_flag, p.status);
+#pragma unroll 1
+        for (int sub = 0; sub < NSUB; ++sub) {
+          const int n = n0 + sub * 128 + q * 32 + lane;  // this lane's output column
+          const float sc = (n < p.N && p.scale) ? p.scale[n] : 1.f;
+          const float bs = (n < p.N && bias) ? to_f32(bias[n]) : 0.f;
+          T* tile = out_tile + sub * BM * 128;
+#pragma unroll 1
+          for (int c = 32 * h; c < BM; c += 64) {
+            float v[32];
+            if (ok) tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
+            if (use_tma) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float o = v[j] * sc + bs;
+                T* e = tile + (c + j) * 128 + q * 32 + lane;
+                if (resid && res_ok) o = to_f32(from_f32<T>(o)) + to_f32(*e);
+                *e = from_f32<T>(o);
+              }
+            } else if (ok && n < p.N) {
+#pragma unroll 4
+              for (int j = 0; j < 32; ++j) {
+                const int m = m0 + c + j;
+                if (m < p.M) {
+                  float o = v[j] * sc + bs;
+                  if (resid) o = to_f32(from_f32<T>(o)) + to_f32(resid[static_cast<long long>(m) * p.N + n]);
+                  y[static_cast<long long>(m) * p.N + n] = from_f32<T>(o);
+                }
+              }
+            }
+          }
+          if (use_tma) {
+            fence_proxy_async();
+            epi_bar();
+            if (threadIdx.x == 96) {
+              if (p.push.world > 0) {
+                for (int d = 0; d < p.push.world; ++d) tma_store_2d(&om.dst[d], out_sa + sub * BM * 256, n0 + sub * 128, m0);
+              } else {
+                tma_store_2d(&om.y, out_sa + sub * BM * 256, n0 + sub * 128, m0);
+              }
+              bulk_commit();
+            }
+          }
+        }
+        if (use_tma && threadIdx.x == 96) {
+          bulk_wait_all();  // stores done (pushed outputs complete before the arrival below)
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+      }
+    } else {
+      // ------------------------------------------------ split-K cluster --
+      float* stage = reinterpret_cast<float*>(gbase + C::kOffStage);
+      const uint32_t stage_sa = base + C::kOffStage;
+      const uint32_t recv_sa = stage_sa + BM * 512;
+      const int crank = static_cast<int>(cluster_ctarank());
+      const int share = (BM + S - 1) / S;
+      const int r0 = min(BM, crank * share);
+      const int r1 = min(BM, r0 + share);
+      const int my_rows = r1 - r0;
+      const int ndst = p.push.world > 0 ? p.push.world : 1;
 #pragma unroll 1
       for (int sub = 0; sub < NSUB; ++sub) {
-        const int nb = n0 + sub * 128 + q * 32;  // first weight row of this warp's 32
-        const int n = nb + lane;                 // this lane's row (before the transpose)
-        const float sc = (!part && n < p.N && p.scale) ? p.scale[n] : 1.f;
-        const float bs = (!part && n < p.N && bias) ? to_f32(bias[n]) : 0.f;
+        if (warp >= 3 && ok) {
 #pragma unroll 1
-        for (int c = 32 * h; c < BM; c += 64) {
-          float v[32];
-          __syncwarp();
-          tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
+          for (int c = 32 * h; c < BM; c += 64) {
+            float v[32];
+            tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) tp[j * 33 + lane] = v[j] * sc + bs;  // [token j][row lane]
-          __syncwarp();
-          const int m = m0 + c + lane;  // this lane's token row after the transpose
-          if (m < p.M && nb < p.N) {
-            float o[32];
+            for (int j = 0; j < 32; ++j) stage[(c + j) * 128 + q * 32 + lane] = v[j];
+          }
+        }
+        fence_proxy_async();  // generic stage writes -> the bulk copies below
+        if (threadIdx.x == 96) mbar_expect_tx(recv_full, (S - 1) * my_rows * 512);
+        PS_TC_TRACE(5 + sub * 4, threadIdx.x == 96);
+        cluster_sync();  // every split staged; every peer's rings idle
+        PS_TC_TRACE(6 + sub * 4, threadIdx.x == 96);
+        if (threadIdx.x == 96) {
+          for (int j = 0; j < S; ++j) {
+            if (j == crank) continue;
+            const int j0 = min(BM, j * share);
+            const int rows = min(BM, j0 + share) - j0;
+            if (rows <= 0) continue;
+            const int slot = crank < j ? crank : crank - 1;  // my slot among j's S-1 senders
+            bulk_s2s(mapa_shared(recv_sa + slot * share * 512, j), stage_sa + j0 * 512, rows * 512,
+                     mapa_shared(recv_full, j));
+          }
+        }
+        const bool got = warp_wait(recv_full, sub & 1, abort_flag, p.status);
+        // thread t owns columns n8 = 8 * (t % 16) of the sub-tile, 22 rows per pass
+        const int n8 = (threadIdx.x & 15) * 8;
+        const int gn = n0 + sub * 128 + n8;
+        if (got && gn < p.N) {
+          const int cnt = min(8, p.N - gn);
+          const bool vec = (p.N % 8) == 0;
+          float sc[8], bs[8];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] = tp[lane * 33 + j];
-            const int cnt = min(32, p.N - nb);
-            if (part) {
-              float* dst = p.part + (static_cast<long long>(split) * p.M + m) * p.N + nb;
-              if (cnt == 32 && (p.N % 4) == 0) {
+          for (int j = 0; j < 8; ++j) {
+            sc[j] = (j < cnt && p.scale) ? p.scale[gn + j] : 1.f;
+            bs[j] = (j < cnt && bias) ? to_f32(bias[gn + j]) : 0.f;
+          }
+#pragma unroll 1
+          for (int m = r0 + (threadIdx.x >> 4); m < r1; m += kThreads / 16) {
+            const int gm = m0 + m;
+            if (gm >= p.M) continue;
+            float acc[8];
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                  *reinterpret_cast<float4*>(dst + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-              } else {
-                for (int j = 0; j < cnt; ++j) dst[j] = o[j];
+            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+            for (int sr = 0; sr < S; ++sr) {  // split order: identical sums on every run
+              const float* src = sr == crank ? stage + m * 128 + n8
+                                             : reinterpret_cast<const float*>(gbase + C::kOffStage + BM * 512) +
+                                                   ((sr < crank ? sr : sr - 1) * share + (m - r0)) * 128 + n8;
+              const float4 a = reinterpret_cast<const float4*>(src)[0];
+              const float4 b = reinterpret_cast<const float4*>(src)[1];
+              acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+              acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+            }
+            const long long off = static_cast<long long>(gm) * p.N + gn;
+            if (vec) {
+              float rv[8];
+              if (resid) unpack8<T>(*reinterpret_cast<const uint4*>(resid + off), rv);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                acc[j] = acc[j] * sc[j] + bs[j];
+                if (resid) acc[j] = to_f32(from_f32<T>(acc[j])) + rv[j];
               }
+              const uint4 pk = pack8<T>(acc);
+              for (int d = 0; d < ndst; ++d)  // push: every rank's slot (peers over NVLink)
+                *reinterpret_cast<uint4*>((p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off) = pk;
             } else {
-              const long long off = static_cast<long long>(m) * p.N + nb;
-              const T* rs = resid ? resid + off : nullptr;
-              const int ndst = p.push.world > 0 ? p.push.world : 1;
-              if (cnt == 32 && (p.N % 8) == 0) {
-                if (rs) {
-                  float rv[32];
 #pragma unroll
-                  for (int j = 0; j < 32; j += 8) unpack8<T>(*reinterpret_cast<const uint4*>(rs + j), rv + j);
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) o[j] = to_f32(from_f32<T>(o[j])) + rv[j];
-                }
-                uint4 pk[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) pk[j] = pack8<T>(o + 8 * j);
-                for (int d = 0; d < ndst; ++d) {  // push: every rank's slot (peers over NVLink)
-                  T* dst = (p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off;
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = pk[j];
-                }
-              } else {
-                for (int d = 0; d < ndst; ++d) {
-                  T* dst = (p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off;
-                  for (int j = 0; j < cnt; ++j) {
-                    float v2 = o[j];
-                    if (rs) v2 = to_f32(from_f32<T>(v2)) + to_f32(rs[j]);
-                    dst[j] = from_f32<T>(v2);
-                  }
+              for (int j = 0; j < 8; ++j) {
+                if (j < cnt) {
+                  float v2 = acc[j] * sc[j] + bs[j];
+                  if (resid) v2 = to_f32(from_f32<T>(v2)) + to_f32(resid[off + j]);
+                  y[off + j] = from_f32<T>(v2);
                 }
               }
             }
           }
         }
+        PS_TC_TRACE(7 + sub * 4, threadIdx.x == 96);
+        cluster_sync();  // slices consumed, stage and receive buffers free again
+        PS_TC_TRACE(8 + sub * 4, threadIdx.x == 96);
       }
     }
   }
@@ -571,61 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
   }
-  if (p.push.world > 0 && p.splits == 1) push_arrive(p.push);
-}
-
-// Split-K finish: y = scale * sum_s part[s] + bias (+ residual), 4 outputs
-// per thread (16-byte partial loads), grid-stride; reads the partials from L2.
-template <typename T>
-__global__ void splitk_reduce_kernel(T* __restrict__ y, const float* __restrict__ part,
-                                     const float* __restrict__ scale, const T* __restrict__ bias,
-                                     const T* __restrict__ resid, int M, int N, int splits,
-                                     const PushTargets push) {
-  const int nq = N / 4;
-  const long long total = static_cast<long long>(M) * nq;
-  const long long plane = static_cast<long long>(M) * N;
-  for (long long it = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; it < total;
-       it += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long m = it / nq;
-    const int n = static_cast<int>(it - m * nq) * 4;
-    const float* src = part + m * N + n;
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
-    int s = 1;
-    for (; s + 3 < splits; s += 4) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(src + s * plane));
-      const float4 b = __ldcg(reinterpret_cast<const float4*>(src + (s + 1) * plane));
-      const float4 c = __ldcg(reinterpret_cast<const float4*>(src + (s + 2) * plane));
-      const float4 d = __ldcg(reinterpret_cast<const float4*>(src + (s + 3) * plane));
-      acc.x += (a.x + b.x) + (c.x + d.x);
-      acc.y += (a.y + b.y) + (c.y + d.y);
-      acc.z += (a.z + b.z) + (c.z + d.z);
-      acc.w += (a.w + b.w) + (c.w + d.w);
-    }
-    for (; s < splits; ++s) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(src + s * plane));
-      acc.x += a.x;
-      acc.y += a.y;
-      acc.z += a.z;
-      acc.w += a.w;
-    }
-    float o[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      o[j] = o[j] * (scale ? scale[n + j] : 1.f) + (bias ? to_f32(bias[n + j]) : 0.f);
-      if (resid) o[j] = to_f32(from_f32<T>(o[j])) + to_f32(resid[m * N + n + j]);
-    }
-    T v4[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v4[j] = from_f32<T>(o[j]);
-    const uint2 u = *reinterpret_cast<const uint2*>(v4);
-    if (push.world > 0) {
-      for (int d = 0; d < push.world; ++d)  // every rank's slot (peers over NVLink)
-        *reinterpret_cast<uint2*>(static_cast<T*>(push.dst[d]) + m * N + n) = u;
-    } else {
-      *reinterpret_cast<uint2*>(y + m * N + n) = u;
-    }
-  }
-  if (push.world > 0) push_arrive(push);
+  if (p.push.world > 0) push_arrive(p.push);
 }
 
 // Re-tile a row-major int8 weight [N][K] into 8 KB blocks [N/128][K/64][128][64]
@@ -732,20 +831,15 @@ Plan plan(int M, int N, int K, bool int8) {
   pl.n_tiles = (N + 128 * pl.nsub - 1) / (128 * pl.nsub);
   const int max_split = pl.k_tiles / 4 > 0 ? pl.k_tiles / 4 : 1;  // >= 4 K tiles per split
   if (splits > max_split) splits = max_split;
+  if (splits > 8) splits = 8;  // one portable cluster per output tile
   if (splits < 1) splits = 1;
-  if (N % 4 != 0) splits = 1;  // the split-K reduction reads 4 outputs at a time
   pl.per_split = (pl.k_tiles + splits - 1) / splits;
   pl.splits = (pl.k_tiles + pl.per_split - 1) / pl.per_split;
   return pl;
 }
 
-size_t ws_bytes(const Plan& pl, int M, int N) {
-  if (pl.splits <= 1) return 0;
-  return static_cast<size_t>(pl.splits) * M * N * 4 + 256;
-}
-
 template <typename T, bool kInt8, int NSUB, int BM>
-int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
+int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl, const OutMaps& om, cudaStream_t s) {
   using C = Cfg<kInt8, NSUB, BM>;
   auto kern = linear_tc_kernel<T, kInt8, NSUB, BM>;
   static bool attr_set = false;  // one attribute call per instantiation
@@ -756,39 +850,93 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, 
     }
     attr_set = true;
   }
-  dim3 grid(pl.n_tiles, pl.m_tiles, pl.splits);
-  kern<<<grid, kThreads, C::kBytes, s>>>(wm, xm, p);
+  // split-K: the fp32 stage plus S-1 received row slices must fit the rings
+  int splits = pl.splits;
+  while (splits > 1 && static_cast<long long>(BM) * 512 + static_cast<long long>(splits - 1) *
+                                                             ((BM + splits - 1) / splits) * 512 > C::kRings)
+    --splits;
+  // ... and all clusters must be resident at once: a cluster needs `splits`
+  // SMs of one GPC, so large clusters can leave a second wave (queried once
+  // per cluster size from the occupancy calculator).
+  static int max_clusters[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  const int tiles = pl.n_tiles * pl.m_tiles;
+  while (splits > 1) {
+    if (max_clusters[splits] == 0) {
+      cudaLaunchConfig_t qc = {};
+      qc.gridDim = dim3(1, 1, splits);
+      qc.blockDim = dim3(kThreads);
+      qc.dynamicSmemBytes = C::kBytes;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 1;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = splits;
+      qc.attrs = qa;
+      qc.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &qc) != cudaSuccess || n < 1) {
+        (void)cudaGetLastError();
+        n = -1;
+      }
+      max_clusters[splits] = n;
+    }
+    if (max_clusters[splits] >= tiles) break;
+    --splits;
+  }
+  if (splits != pl.splits) {
+    pl.per_split = (pl.k_tiles + splits - 1) / splits;
+    pl.splits = (pl.k_tiles + pl.per_split - 1) / pl.per_split;
+    p.k_tiles_per_split = pl.per_split;
+    p.splits = pl.splits;
+  }
+  p.tma_out = (pl.splits == 1 && (p.N % 8) == 0) ? 1 : 0;
+#ifdef PS_TRACE
+  fprintf(stderr, "[linear_tc] M=%d N=%d K=%d nsub=%d bm=%d splits=%d tiles=%d max_clusters(splits)=%d\n", p.M, p.N,
+          p.K, NSUB, BM, pl.splits, tiles, pl.splits > 1 ? max_clusters[pl.splits] : 0);
+#endif
+  // The split-K CTAs of one output tile form a (1, 1, splits) cluster and
+  // reduce their partial tiles through distributed shared memory.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.n_tiles, pl.m_tiles, pl.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = pl.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = pl.splits > 1 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wm, xm, p, om);
+  if (e != cudaSuccess) {
+    ps_host::set_error("linear_tc: launch failed: %s", cudaGetErrorString(e));
+    return PS_ERR_CUDA;
+  }
   ps_host::count_launch();
-  int rc = ps_host::check_launch("linear_tc");
-  if (rc != PS_OK || pl.splits == 1) return rc;
-  const long long items = static_cast<long long>(p.M) * (p.N / 4);
-  long long blocks = (items + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  splitk_reduce_kernel<T><<<static_cast<int>(blocks), 256, 0, s>>>(
-      static_cast<T*>(p.y), p.part, p.scale, static_cast<const T*>(p.bias), static_cast<const T*>(p.resid), p.M,
-      p.N, pl.splits, p.push);
-  ps_host::count_launch();
-  return ps_host::check_launch("linear_tc(split-K reduce)");
+  return ps_host::check_launch("linear_tc");
 }
 
 template <typename T, bool kInt8, int NSUB>
-int launch_nsub(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
+int launch_nsub(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, const OutMaps& om,
+                cudaStream_t s) {
   switch (pl.bm) {
-    case 32: return launch_cfg<T, kInt8, NSUB, 32>(wm, xm, p, pl, s);
-    case 64: return launch_cfg<T, kInt8, NSUB, 64>(wm, xm, p, pl, s);
-    case 128: return launch_cfg<T, kInt8, NSUB, 128>(wm, xm, p, pl, s);
-    case 192: return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, s);
+    case 32: return launch_cfg<T, kInt8, NSUB, 32>(wm, xm, p, pl, om, s);
+    case 64: return launch_cfg<T, kInt8, NSUB, 64>(wm, xm, p, pl, om, s);
+    case 128: return launch_cfg<T, kInt8, NSUB, 128>(wm, xm, p, pl, om, s);
+    case 192: return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, om, s);
     default:
       // int8 with 256-row slabs caps the token tile at 192 (TMEM holds the
       // accumulators and two widened A stages); the planner never asks more.
-      if constexpr (kInt8 && NSUB == 2) return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, s);
-      else return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, s);
+      if constexpr (kInt8 && NSUB == 2) return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, om, s);
+      else return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, om, s);
   }
 }
 
 template <typename T, bool kInt8>
-int launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, cudaStream_t s) {
-  return pl.nsub == 2 ? launch_nsub<T, kInt8, 2>(wm, xm, p, pl, s) : launch_nsub<T, kInt8, 1>(wm, xm, p, pl, s);
+int launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, const OutMaps& om,
+             cudaStream_t s) {
+  return pl.nsub == 2 ? launch_nsub<T, kInt8, 2>(wm, xm, p, pl, om, s) : launch_nsub<T, kInt8, 1>(wm, xm, p, pl, om, s);
 }
 
 }  // namespace
@@ -801,11 +949,7 @@ extern "C" PS_API int ps_debug_tc_trace(unsigned long long* host, int n) {
 
 namespace ps_host {
 
-size_t linear_tc_workspace(int M, int N, int K) {
-  const size_t a = ws_bytes(plan(M, N, K, true), M, N);
-  const size_t b = ws_bytes(plan(M, N, K, false), M, N);
-  return a > b ? a : b;
-}
+size_t linear_tc_workspace(int, int, int) { return 0; }  // split-K reduces on chip (clusters)
 
 size_t tiled_int8_bytes(int N, int K) {
   return static_cast<size_t>((N + 127) / 128) * ((K + kBK - 1) / kBK) * 8192;
@@ -848,19 +992,12 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   p.k_tiles_per_split = pl.per_split;
   p.splits = pl.splits;
   if (push) {
-    // the push path writes whole 16-byte (epilogue) / 8-byte (split-K) groups
+    // the push path stores whole 16-byte groups of outputs, residual-free
     if (resid || bias || N % 8 != 0) return PS_ERR_UNSUPPORTED;
     p.push = *push;
   }
-  if (pl.splits > 1) {
-    const size_t need = ws_bytes(pl, M, N);
-    if (!workspace || workspace_bytes < need) {
-      set_error("linear: split-K workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-      return PS_ERR_INVALID;
-    }
-    p.part = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) &
-                                      ~static_cast<uintptr_t>(255));
-  }
+  (void)workspace;
+  (void)workspace_bytes;
   const CUtensorMapDataType xdt =
       dtype == PS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int bn = 128 * pl.nsub;
@@ -869,13 +1006,27 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   if (int8 && w_tiled) wm = xm;  // unused: the weight arrives by contiguous bulk copies
   else if (int8) ok = ok && make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, kBK, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
   else ok = ok && make_map(&wm, w, xdt, 2, N, K, kBK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  // Output maps (box 128 columns x BM tokens). Built whenever N % 8 == 0;
+  // the kernel uses them only when the tile is not split.
+  OutMaps om;
+  std::memset(&om, 0, sizeof(om));
+  if (ok && N % 8 == 0) {
+    if (push) {
+      for (int d = 0; d < push->world; ++d)
+        ok = ok && make_map(&om.dst[d], push->dst[d], xdt, 2, push->max_tokens, N, 128, pl.bm,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+      ok = ok && make_map(&om.y, y, xdt, 2, M, N, 128, pl.bm, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    if (resid) ok = ok && make_map(&om.res, resid, xdt, 2, M, N, 128, pl.bm, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   if (!ok) {
     set_error("linear: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
     return PS_ERR_CUDA;
   }
   if (dtype == PS_BF16)
-    return int8 ? launch_t<__nv_bfloat16, true>(wm, xm, p, pl, s) : launch_t<__nv_bfloat16, false>(wm, xm, p, pl, s);
-  return int8 ? launch_t<__half, true>(wm, xm, p, pl, s) : launch_t<__half, false>(wm, xm, p, pl, s);
+    return int8 ? launch_t<__nv_bfloat16, true>(wm, xm, p, pl, om, s) : launch_t<__nv_bfloat16, false>(wm, xm, p, pl, om, s);
+  return int8 ? launch_t<__half, true>(wm, xm, p, pl, om, s) : launch_t<__half, false>(wm, xm, p, pl, om, s);
 }
 
 }  // namespace ps_host

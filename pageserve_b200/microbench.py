@@ -163,13 +163,76 @@ def bench_attn_prefill(T=512, start=0, Hq=16, Hkv=2, D=128, bs=16, iters=20, see
     return {"case": "attn_prefill", "T": T, "start": start, "us": ms * 1e3, "tflops": flops / ms / 1e9}
 
 
+def bench_tp_reduce(M=576, H=2048, K_full=2048, iters=20, warmup=3, seed=0):
+    """Row-parallel linear + all-reduce + RMSNorm of one layer position under
+    tensor parallelism (run under torchrun, one rank per GPU): NCCL all_reduce
+    vs the fused peer-memory push, vs the linear + norm alone (no exchange).
+    Device time per iteration, max over ranks."""
+    import torch.distributed as dist
+
+    from .comm import FusedAllReduce
+    from .model import rms_norm_fused
+    from .quantization import LinearWorkspace, QuantizedWeight
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + rank)
+    K = K_full // world
+    w = QuantizedWeight((torch.randn(H, K, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    resid = torch.randn(M, H, device=dev, generator=torch.Generator(device=dev).manual_seed(seed)).to(torch.bfloat16)
+    nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    ws = LinearWorkspace()
+    comm = FusedAllReduce.create(rank, world, M, H, torch.bfloat16, dev)
+    xr = resid.clone()
+
+    def nccl():
+        y = w.linear(x, residual=xr if rank == 0 else None, workspace=ws)
+        dist.all_reduce(y)
+        rms_norm_fused(y, nw, 1e-6)
+
+    it = [0]
+
+    def fused():  # the sets must alternate, as o_proj / down_proj do in a layer
+        s_ = it[0] & 1
+        it[0] += 1
+        comm.linear_push(x, w, s_, workspace=ws)
+        comm.allreduce_rmsnorm(xr, nw, 1e-6, s_)
+
+    def local():
+        y = w.linear(x, residual=xr, workspace=ws)
+        rms_norm_fused(y, nw, 1e-6)
+
+    def push_only():  # producer side alone (flags only accumulate; nothing waits)
+        comm.linear_push(x, w, 0, workspace=ws)
+
+    def linear_only():
+        w.linear(x, workspace=ws)
+
+    def allreduce_only():
+        dist.all_reduce(xr)
+
+    out = {"case": "tp_reduce", "world": world, "M": M, "H": H, "K_shard": K}
+    for name, fn in (("nccl_us", nccl), ("fused_us", fused), ("local_us", local), ("push_only_us", push_only),
+                     ("linear_only_us", linear_only), ("nccl_allreduce_only_us", allreduce_only)):
+        dist.barrier()
+        ms = _time(fn, iters, warmup)
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = t.item() * 1e3
+    torch.cuda.synchronize()
+    dist.barrier()
+    comm.close()
+    return out
+
+
 SWEEP_NK = [(2560, 2048), (2048, 2048), (22016, 2048), (2048, 11008)]
 SWEEP_M = [1, 8, 64, 256, 2048]
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["linear", "sweep", "attn", "prefill"])
+    ap.add_argument("what", choices=["linear", "sweep", "attn", "prefill", "tp"])
     ap.add_argument("--M", type=int, default=576)
     ap.add_argument("--N", type=int, default=22016)
     ap.add_argument("--K", type=int, default=2048)
@@ -179,6 +242,24 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
     torch.cuda.init()
+    if a.what == "tp":  # under torchrun: one rank per GPU
+        import datetime
+        import os
+
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        for m, kf in ((576, 2048), (576, 11008), (64, 2048), (64, 11008)):
+            r = bench_tp_reduce(M=m, K_full=kf, iters=a.iters, warmup=a.warmup)
+            if dist.get_rank() == 0:
+                print(json.dumps(r), flush=True)
+        from . import _lib
+        _lib.raise_on_device_error()
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
     if a.what == "linear":
         print(json.dumps(bench_linear(a.M, a.N, a.K, a.iters, bf16_weight=a.bf16_weight, warmup=a.warmup,
                                       tiled=not a.row_major)))

@@ -533,6 +533,13 @@ class StepGraph:
         logits = self.m._forward(self.ids_dev, self.meta, last)
         return logits, self.m.next_tokens(logits)
 
+    def release(self) -> None:
+        """Drop the captured graph (before destroy_process_group when it
+        holds NCCL calls)."""
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
+
     def replay(self) -> None:
         """Re-run the captured step on the current device buffers."""
         self.graph.replay()

@@ -140,7 +140,12 @@ def test_consumer_wait_times_out_without_producer():
         rank.allreduce_rmsnorm(x, w, 1e-6, 1)
         torch.cuda.synchronize()
         assert _lib.device_status(clear=True) == 4  # kErrTimeout
-        # still usable: a normal push/consume round afterwards
+        # the buffer is marked broken: the next wait gives up at once
+        rank.allreduce_rmsnorm(x, w, 1e-6, 0)
+        torch.cuda.synchronize()
+        assert _lib.device_status(clear=True) == 4
+        rank.reset()
+        # still usable after re-zeroing: a normal push/consume round
         xin = torch.randn(4, 64, device=dev).to(torch.bfloat16)
         wt = (torch.randn(256, 64, device=dev) * 0.1).to(torch.bfloat16)
         rank.linear_push(xin, wt, 1)
