@@ -182,7 +182,7 @@ def kernel_breakdown(m, w, peaks):
     import torch
 
     from pageserve_b200.paged_attention import AttentionWorkspace, paged_attention
-    from pageserve_b200.quantization import LinearWorkspace, linear16, w8a16_linear
+    from pageserve_b200.quantization import LinearWorkspace, linear16, linear_swiglu, w8a16_linear
 
     dev = m.device
     T = N_DECODE + PREFILL
@@ -194,27 +194,30 @@ def kernel_breakdown(m, w, peaks):
     ws = LinearWorkspace()
     res = {}
 
-    def lin(name, x, get_w):
+    def lin(name, x, get_w, swiglu=False):
         outs = {}
         ctr = [0]
 
         def f():
             wgt = get_w(m.fused[ctr[0] % L])
             ctr[0] += 1
-            outs["y"] = w8a16_linear(x, wgt.q, wgt.scale, workspace=ws, q_tiled=wgt.tiled())
+            if swiglu:  # the gate|up linear with SiLU*up in its epilogue, as the step runs it
+                outs["y"] = linear_swiglu(x, wgt)
+            else:
+                outs["y"] = w8a16_linear(x, wgt.q, wgt.scale, workspace=ws, q_tiled=wgt.tiled())
         f()
         ms = time_events(f, 2 * L)
         wgt = get_w(m.fused[0])
         N, K = wgt.q.shape
         M = x.shape[0]
         flops = 2.0 * M * N * K
-        byts = N * K + 4 * N + 2 * M * K + 2 * M * N
+        byts = N * K + 4 * N + 2 * M * K + 2 * M * (N // 2 if swiglu else N)
         res[name] = {"ms": ms, "M": M, "N": N, "K": K, "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6,
                      "flops": flops, "bytes": byts}
 
     lin("qkv", x_h, lambda f: f.qkv)
     lin("o_proj", x_a, lambda f: f.o)
-    lin("gate_up", x_h, lambda f: f.gate_up)
+    lin("gate_up", x_h, lambda f: f.gate_up, swiglu=True)
     lin("down", x_i, lambda f: f.down)
     # lm_head on the 65 sampled rows
     xl = torch.randn(N_DECODE + 1, H, device=dev, dtype=torch.bfloat16)

@@ -208,6 +208,17 @@ PS_API int ps_embedding(void* out_dev, const int64_t* ids_dev, const void* table
  * the maximum of each row; logits (M, V) in dtype; out int32 [M]. */
 PS_API int ps_argmax(int32_t* out_dev, const void* logits_dev, int M, int V, int ld, int dtype, ps_stream_t stream);
 
+/* Gate/up projection fused with SwiGLU (engine/model.py:188-190:
+ * F.silu(F.linear(x, gate_w)) * F.linear(x, up_w)): one tensor-core linear
+ * over the row-interleaved weight [2I][K] (row 2i = gate row i, row 2i+1 =
+ * up row i; int8 tiled with its per-row scale as ps_w8a16_linear_tiled, or
+ * a 16-bit weight with w_tiled NULL), whose epilogue rounds gate and up to
+ * dtype and writes y[m][i] = silu(gate) * up (float32 math, one rounding),
+ * y (M, I) with N2 = 2I a multiple of 16. Same values as the gate|up linear
+ * followed by ps_silu_mul. */
+PS_API int ps_linear_swiglu(void* y_dev, const void* x_dev, const void* w_dev, int wdtype, const int8_t* w_tiled_dev,
+                            const float* scale_dev, int M, int N2, int K, int dtype, ps_stream_t stream);
+
 /* ------------------------------------- (e) fused tensor-parallel all-reduce
  *
  * Replaces the dist.all_reduce(partial, SUM) after each row-parallel linear

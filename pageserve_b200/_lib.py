@@ -54,6 +54,7 @@ _SIGNATURES = {
     "ps_rope_qkv_write_kv": (c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "ps_embedding": (c_int, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "ps_argmax": (c_int, [_P, _P, _I, _I, _I, _I, _P]),
+    "ps_linear_swiglu": (c_int, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P]),
     "ps_comm_buffer_bytes": (c_size_t, [_I, _I, _I, _I]),
     "ps_comm_alloc": (c_int, [_P, c_size_t]),
     "ps_comm_free": (c_int, [_P]),

@@ -125,6 +125,12 @@ PS_DEVICE float warp_max(float v) {
   return v;
 }
 
+// silu(g) * u in float32 (F.silu(gate) * up, engine/model.py:190), shared by
+// the standalone kernel and the gate|up linear's epilogue so both give the
+// same values: g / (1 + e^-g) with the fast exponential and divide (relative
+// error ~1e-6, far below the bf16/f16 output rounding; 0 for g -> -inf).
+PS_DEVICE float silu_mul_f32(float g, float u) { return __fdividef(g, 1.f + __expf(-g)) * u; }
+
 PS_DEVICE void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }

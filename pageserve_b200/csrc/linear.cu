@@ -120,6 +120,30 @@ int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_til
   return r2;
 }
 
+int ps_linear_swiglu(void* y, const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale,
+                     int M, int N2, int K, int dtype, ps_stream_t stream) {
+  const bool int8 = wdtype == PS_I8;
+  if (M < 0 || N2 <= 0 || K <= 0 || !y || !x || (int8 ? (!w_tiled || !scale) : !w)) {
+    ps_host::set_error("linear_swiglu: invalid arguments (M=%d N2=%d K=%d)", M, N2, K);
+    return PS_ERR_INVALID;
+  }
+  if (M == 0) return PS_OK;
+  if ((dtype != PS_BF16 && dtype != PS_F16) || (!int8 && wdtype != dtype)) {
+    ps_host::set_error("linear_swiglu: bf16/f16 activations with int8 or same-type weights");
+    return PS_ERR_UNSUPPORTED;
+  }
+  if (N2 % 16 != 0 || K % 16 != 0 || !ps_host::aligned(y, 16) || !ps_host::aligned(x, 16) ||
+      !ps_host::aligned(w, 16) || !ps_host::aligned(w_tiled, 16) || !ps_host::aligned(scale, 16)) {
+    ps_host::set_error("linear_swiglu: 2*intermediate must be a multiple of 16, K of 16, tensors 16-byte aligned");
+    return PS_ERR_INVALID;
+  }
+  const int rc = ps_host::linear_tc(y, x, int8 ? static_cast<const void*>(w_tiled) : w, wdtype, scale, nullptr,
+                                    nullptr, M, N2, K, dtype, nullptr, 0, reinterpret_cast<cudaStream_t>(stream),
+                                    int8 ? w_tiled : nullptr, nullptr, true);
+  if (rc == PS_ERR_UNSUPPORTED) ps_host::set_error("linear_swiglu: no tensor-core configuration for this shape");
+  return rc;
+}
+
 int ps_linear(void* y, const void* x, const void* w, const void* bias, const void* resid, int M, int N, int K,
               int dtype, void* ws, size_t ws_bytes, ps_stream_t stream) {
   return linear_any(y, x, w, dtype, nullptr, bias, resid, M, N, K, dtype, ws, ws_bytes, stream, "linear");

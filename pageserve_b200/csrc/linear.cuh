@@ -10,7 +10,8 @@ int linear_simt(void* y, const void* x, const void* w, int wdtype, const float* 
 // when the shape has no tensor-core configuration.
 int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
               const void* resid, int M, int N, int K, int dtype, void* workspace, size_t workspace_bytes,
-              cudaStream_t s, const int8_t* w_tiled = nullptr, const ps::PushTargets* push = nullptr);
+              cudaStream_t s, const int8_t* w_tiled = nullptr, const ps::PushTargets* push = nullptr,
+              bool swiglu = false);
 // int8 weight re-tiled into 8 KB blocks [N/128][K/64][128][64] for linear_tc.
 size_t tiled_int8_bytes(int N, int K);
 int tile_int8(int8_t* dst, const int8_t* src, int N, int K, cudaStream_t s);

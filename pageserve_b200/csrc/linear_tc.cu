@@ -304,6 +304,7 @@ struct TcParams {
   int k_tiles_per_split;
   int splits;       // split-K CTAs per output tile = cluster size along z (1: no cluster)
   int tma_out;      // splits == 1 and N % 8 == 0: outputs leave by TMA stores (OutMaps)
+  int swiglu;       // rows interleaved (2i gate_i, 2i+1 up_i): y[m][i] = silu(gate) * up, width N / 2
   PushTargets push;  // world > 0: the final output goes to every rank's receive slot instead of y
 };
 
@@ -581,7 +582,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 32 * h; c < BM; c += 64) {
             float v[32];
             if (ok) tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
-            if (use_tma) {
+            if (use_tma && p.swiglu) {
+              // lanes 2k / 2k+1 hold gate / up of intermediate channel
+              // (n0 + sub*128 + q*32)/2 + k: each rounded to dtype (the
+              // linear's output), then silu(gate) * up in float32.
+              T* tile2 = out_tile + sub * BM * 64;  // [BM][64] per sub-tile
+              // The pair splits the 32 tokens: the even lane finishes tokens
+              // 0..15, the odd lane 16..31 (one exchange per token pair).
+              const bool odd = lane & 1;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float mine_lo = to_f32(from_f32<T>(v[j] * sc + bs));
+                const float mine_hi = to_f32(from_f32<T>(v[j + 16] * sc + bs));
+                const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_lo : mine_hi, 1);
+                const float gate = odd ? other : mine_lo;
+                const float up = odd ? mine_hi : other;
+                tile2[(c + j + (odd ? 16 : 0)) * 64 + q * 16 + (lane >> 1)] = from_f32<T>(silu_mul_f32(gate, up));
+              }
+            } else if (use_tma) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 float o = v[j] * sc + bs;
@@ -605,7 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async();
             epi_bar();
             if (threadIdx.x == 96) {
-              if (p.push.world > 0) {
+              if (p.swiglu) {
+                tma_store_2d(&om.y, out_sa + sub * BM * 128, (n0 + sub * 128) / 2, m0);
+              } else if (p.push.world > 0) {
                 for (int d = 0; d < p.push.world; ++d) tma_store_2d(&om.dst[d], out_sa + sub * BM * 256, n0 + sub * 128, m0);
               } else {
                 tma_store_2d(&om.y, out_sa + sub * BM * 256, n0 + sub * 128, m0);
@@ -889,7 +909,7 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl
     p.k_tiles_per_split = pl.per_split;
     p.splits = pl.splits;
   }
-  p.tma_out = (pl.splits == 1 && (p.N % 8) == 0) ? 1 : 0;
+  p.tma_out = (pl.splits == 1 && (p.N % 8) == 0) ? 1 : 0;  // SwiGLU implies N % 16 == 0
 #ifdef PS_TRACE
   fprintf(stderr, "[linear_tc] M=%d N=%d K=%d nsub=%d bm=%d splits=%d tiles=%d max_clusters(splits)=%d\n", p.M, p.N,
           p.K, NSUB, BM, pl.splits, tiles, pl.splits > 1 ? max_clusters[pl.splits] : 0);
@@ -967,8 +987,10 @@ int tile_int8(int8_t* dst, const int8_t* src, int N, int K, cudaStream_t s) {
 
 int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* scale, const void* bias,
               const void* resid, int M, int N, int K, int dtype, void* workspace, size_t workspace_bytes,
-              cudaStream_t s, const int8_t* w_tiled, const ps::PushTargets* push) {
+              cudaStream_t s, const int8_t* w_tiled, const ps::PushTargets* push, bool swiglu) {
   if (dtype != PS_BF16 && dtype != PS_F16) return PS_ERR_UNSUPPORTED;
+  // SwiGLU epilogue: TMA-stored [M][N/2] output, no residual, no push, no split
+  if (swiglu && (resid || push || N % 16 != 0)) return PS_ERR_UNSUPPORTED;
   const bool int8 = wdtype == PS_I8;
   if (!int8 && wdtype != dtype) return PS_ERR_UNSUPPORTED;
   // TMA: global row strides must be multiples of 16 bytes; the epilogue's
@@ -976,7 +998,11 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   if (K % 16 != 0 || !aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !aligned(resid, 16) ||
       !aligned(bias, 16) || !aligned(scale, 16) || !aligned(w_tiled, 16))
     return PS_ERR_UNSUPPORTED;
-  const Plan pl = plan(M, N, K, int8);
+  Plan pl = plan(M, N, K, int8);
+  if (swiglu && pl.splits > 1) {  // the SwiGLU pairs are finished in the (unsplit) TMA epilogue
+    pl.splits = 1;
+    pl.per_split = pl.k_tiles;
+  }
   TcParams p{};
   p.wt = int8 ? w_tiled : nullptr;
   p.n_blocks = (N + 127) / 128;
@@ -991,6 +1017,7 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   p.k_tiles = pl.k_tiles;
   p.k_tiles_per_split = pl.per_split;
   p.splits = pl.splits;
+  p.swiglu = swiglu ? 1 : 0;
   if (push) {
     // the push path stores whole 16-byte groups of outputs, residual-free
     if (resid || bias || N % 8 != 0) return PS_ERR_UNSUPPORTED;
@@ -1011,7 +1038,9 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   OutMaps om;
   std::memset(&om, 0, sizeof(om));
   if (ok && N % 8 == 0) {
-    if (push) {
+    if (swiglu) {
+      ok = ok && make_map(&om.y, y, xdt, 2, M, N / 2, 64, pl.bm, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else if (push) {
       for (int d = 0; d < push->world; ++d)
         ok = ok && make_map(&om.dst[d], push->dst[d], xdt, 2, push->max_tokens, N, 128, pl.bm,
                             CU_TENSOR_MAP_SWIZZLE_NONE);

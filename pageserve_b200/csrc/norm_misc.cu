@@ -180,7 +180,7 @@ __global__ void silu_mul_kernel(T* __restrict__ out, const T* __restrict__ gu, i
     unpack8<T>(gvec, g);
     unpack8<T>(uvec, u);
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) o[i] = g[i] / (1.f + expf(-g[i])) * u[i];
+    for (int i = 0; i < VEC; ++i) o[i] = silu_mul_f32(g[i], u[i]);
     reinterpret_cast<uint4*>(out + m * I)[c] = pack8<T>(o);
   }
 }

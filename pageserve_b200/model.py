@@ -25,7 +25,7 @@ import torch
 from . import _lib
 from .batch import attention_runs, pack_metadata
 from .paged_attention import AttentionWorkspace, paged_attention
-from .quantization import LinearWorkspace, QuantizedWeight, linear16, w8a16_linear
+from .quantization import LinearWorkspace, QuantizedWeight, linear16, linear_swiglu, w8a16_linear
 
 Weight = torch.Tensor | QuantizedWeight
 
@@ -122,7 +122,7 @@ class FusedLayer:
     qkv: Weight
     qkv_b: torch.Tensor
     o: Weight
-    gate_up: Weight
+    gate_up: Weight  # rows interleaved: 2i = gate row i, 2i+1 = up row i (the SwiGLU linear's layout)
     down: Weight
 
 
@@ -131,6 +131,16 @@ def _cat_weights(ws: list[Weight], dtype) -> Weight:
         return QuantizedWeight.from_quantized(torch.cat([w.q for w in ws], 0), torch.cat([w.scale for w in ws], 0),
                                               dtype)
     return torch.cat(ws, 0).contiguous()
+
+
+def _interleave_rows(a: Weight, b: Weight, dtype) -> Weight:
+    """Rows a0, b0, a1, b1, ... (per-row scales travel with their rows, so
+    this is exact for int8 weights)."""
+    def il(x, y):
+        return torch.stack([x, y], dim=1).reshape(2 * x.shape[0], *x.shape[1:]).contiguous()
+    if isinstance(a, QuantizedWeight):
+        return QuantizedWeight.from_quantized(il(a.q, b.q), il(a.scale, b.scale), dtype)
+    return il(a, b)
 
 
 class StepMeta:
@@ -303,7 +313,7 @@ class PagedCausalLM:
             self.fused.append(FusedLayer(
                 input_ln=lw.input_ln, post_ln=lw.post_ln,
                 qkv=_cat_weights([lw.q_w, lw.k_w, lw.v_w], dtype), qkv_b=qkv_b, o=lw.o_w,
-                gate_up=_cat_weights([lw.gate_w, lw.up_w], dtype), down=lw.down_w))
+                gate_up=_interleave_rows(lw.gate_w, lw.up_w, dtype), down=lw.down_w))
         for fl in self.fused:  # kernel-side tiled int8 copies, built before any graph capture
             for w in (fl.qkv, fl.o, fl.gate_up, fl.down):
                 if isinstance(w, QuantizedWeight):
@@ -399,10 +409,7 @@ class PagedCausalLM:
                 if self.tp is not None:
                     self.tp.all_reduce_(x)
                 h = rms_norm_fused(x, fl.post_ln, self.rms_eps)
-            gu = self._linear(h, fl.gate_up)
-            act = torch.empty((T, self.intermediate_size), dtype=self.dtype, device=self.device)
-            _lib.check(lib.ps_silu_mul(act.data_ptr(), gu.data_ptr(), T, self.intermediate_size,
-                                       _lib.dtype_code(self.dtype), stream), "silu_mul")
+            act = linear_swiglu(h, fl.gate_up)  # silu(gate) * up in the gate|up linear's epilogue
             if comm is not None:
                 comm.linear_push(act, fl.down, 1, workspace=self.lin_ws)
                 pending = True

@@ -159,6 +159,31 @@ def linear16(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     return out
 
 
+def linear_swiglu(x: torch.Tensor, weight, out: torch.Tensor | None = None) -> torch.Tensor:
+    """F.silu(F.linear(x, gate_w)) * F.linear(x, up_w) (engine/model.py:188-190)
+    in one tensor-core linear over the row-interleaved gate|up weight
+    (row 2i = gate row i, row 2i+1 = up row i): ``weight`` is a
+    QuantizedWeight of that [2I][K] matrix or a bf16/f16 tensor. Returns
+    (..., I)."""
+    _lib.require_cuda(x)
+    lib = _lib.load()
+    if isinstance(weight, QuantizedWeight):
+        N2, K = weight.q.shape
+        w_ptr, wdt, wt_ptr, sc_ptr = weight.q.data_ptr(), _lib.PS_I8, weight.tiled().data_ptr(), \
+            weight.scale.data_ptr()
+    else:
+        N2, K = weight.shape
+        w_ptr, wdt, wt_ptr, sc_ptr = weight.data_ptr(), _lib.dtype_code(weight.dtype), None, None
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((*lead, N2 // 2), dtype=x.dtype, device=x.device)
+    _lib.check(lib.ps_linear_swiglu(out.data_ptr(), x2.data_ptr(), w_ptr, wdt, wt_ptr, sc_ptr, M, N2, K,
+                                    _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device)), "linear_swiglu")
+    return out
+
+
 class QuantizedWeight:
     """engine/quantization.py:30-50, same attributes; ``linear`` runs the
     fused W8A16 kernel."""

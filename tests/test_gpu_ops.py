@@ -371,3 +371,52 @@ def test_w8a16_linear_tiled_matches_oracle(dev, M, NK):
                      q_tiled=tile_int8_weight(qd))
     ref = ops.quantized_linear(ops.round_bf16(x), q, scale, ops.round_bf16(b)) + ops.round_bf16(r)
     assert rel_err(y.float().cpu().numpy(), ref) < REL_TOL
+
+
+@pytest.mark.parametrize("M", [1, 7, 64, 576])
+@pytest.mark.parametrize("IK", [(11008, 2048), (160, 256), (1376, 2048), (896, 640)])
+def test_linear_swiglu_matches_oracle(dev, M, IK):
+    """engine/model.py:188-190: silu(gate) * up from one linear over the
+    row-interleaved gate|up int8 weight; also equal to the unfused gate|up
+    linear followed by ps_silu_mul (same roundings) within the bf16 tolerance."""
+    from pageserve_b200 import _lib
+    from pageserve_b200.model import _interleave_rows
+    from pageserve_b200.quantization import QuantizedWeight, linear_swiglu, w8a16_linear
+    I, K = IK
+    rng = np.random.default_rng(M * 7 + I)
+    qg = rng.integers(-127, 128, size=(I, K)).astype(np.int8)
+    qu = rng.integers(-127, 128, size=(I, K)).astype(np.int8)
+    sg = rng.uniform(1e-3, 1e-2, size=(I, 1)).astype(np.float32)
+    su = rng.uniform(1e-3, 1e-2, size=(I, 1)).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32) * 0.5
+    xb = _bf16(x, dev)
+    wg = QuantizedWeight.from_quantized(torch.from_numpy(qg).to(dev), torch.from_numpy(sg).to(dev), torch.bfloat16)
+    wu = QuantizedWeight.from_quantized(torch.from_numpy(qu).to(dev), torch.from_numpy(su).to(dev), torch.bfloat16)
+    w_il = _interleave_rows(wg, wu, torch.bfloat16)
+    y = linear_swiglu(xb, w_il)
+    g = ops.round_bf16(ops.quantized_linear(ops.round_bf16(x), qg, sg))
+    u = ops.round_bf16(ops.quantized_linear(ops.round_bf16(x), qu, su))
+    ref = ops.silu(g) * u
+    assert y.shape == (M, I)
+    assert rel_err(y.float().cpu().numpy(), ref) < REL_TOL
+    # unfused device path: gate|up linear, then ps_silu_mul
+    gu = w8a16_linear(xb, torch.cat([wg.q, wu.q]), torch.cat([wg.scale, wu.scale]))
+    act = torch.empty(M, I, dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.load().ps_silu_mul(act.data_ptr(), gu.data_ptr(), M, I, _lib.PS_BF16, _lib.stream_ptr(dev)),
+               "silu_mul")
+    torch.cuda.synchronize()
+    assert rel_err(y.float().cpu().numpy(), act.float().cpu().numpy()) < 1e-2
+
+
+def test_linear_swiglu_bf16_weight(dev):
+    from pageserve_b200.model import _interleave_rows
+    from pageserve_b200.quantization import linear_swiglu
+    I, K, M = 384, 512, 40
+    rng = np.random.default_rng(3)
+    wg = rng.standard_normal((I, K), dtype=np.float32) * 0.05
+    wu = rng.standard_normal((I, K), dtype=np.float32) * 0.05
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    y = linear_swiglu(_bf16(x, dev), _interleave_rows(_bf16(wg, dev), _bf16(wu, dev), torch.bfloat16))
+    g = ops.round_bf16(ops.linear(ops.round_bf16(x), ops.round_bf16(wg)))
+    u = ops.round_bf16(ops.linear(ops.round_bf16(x), ops.round_bf16(wu)))
+    assert rel_err(y.float().cpu().numpy(), ops.silu(g) * u) < REL_TOL
