@@ -20,6 +20,7 @@
 #include <cudaTypedefs.h>
 
 #include <cfloat>
+#include <cstdlib>
 #include <climits>
 #include <mutex>
 
@@ -32,7 +33,7 @@ using namespace ps;
 constexpr int kThreads = 128;
 constexpr int kWarps = 4;
 constexpr int kKT = 64;       // keys per shared-memory tile
-constexpr int kStages = 2;
+constexpr int kStages = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnParams {
@@ -626,17 +627,30 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
   WarpState<D> st;
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
+    // The block-table entries of this split are fetched 32 at a time, one per
+    // lane, ahead of the TMA issue (a dependent table load per block would
+    // serialise the ring behind global-memory latency).
+    const int blk_last = (kv_end - 1) / 16;
+    int tab = 0, tab_base = INT_MIN;
     for (int i = 0; i < ntiles; ++i) {
       const int s = i % kTmaStages;
       if (i >= kTmaStages && !warp_wait_a(empty(s), ((i / kTmaStages) - 1) & 1, abort_flag, p.status)) break;
+      const int t0 = kv_begin + i * kTmaTile;
+      const int blk0 = t0 / 16;
+      if (blk0 + 3 > tab_base + 31) {
+        tab_base = blk0;
+        tab = blk0 + lane <= blk_last ? table[blk0 + lane] : 0;
+      }
+      int physj[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) physj[j] = __shfl_sync(0xffffffffu, tab, blk0 - tab_base + j);
       if (lane == 0) {
-        const int t0 = kv_begin + i * kTmaTile;
         const int nblk = min(4, (kv_end - t0 + 15) / 16);
         mbar_expect_tx_a(full(s), nblk * 4 * 2048);
         const uint32_t kst = base + s * kTmaStageBytes;
         const uint32_t vst = kst + kTmaStageBytes / 2;
         for (int j = 0; j < nblk; ++j) {
-          int phys = table[(t0 + 16 * j) / 16];
+          int phys = physj[j];
           if (phys < 0 || phys >= p.num_blocks) {
             record_error(p.status, kErrBlockId);
             phys = 0;  // keep the transaction count; the output is flagged invalid
@@ -836,7 +850,8 @@ void plan_splits(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int 
   const long long ctas = static_cast<long long>(num_seqs) * Hkv;
   // head_dim 128 runs the TMA kernel (2 CTAs per SM with a deep ring): about
   // 1.5 waves of long splits; the cp.async kernel wants many short ones.
-  const long long target = D == 128 ? 148LL * 2 * 3 / 2 : 148LL * 3 * 4;
+  long long target = D == 128 ? 148LL * 2 * 3 / 2 : 148LL * 3 * 4;
+  if (const char* env = std::getenv("PS_ATTN_DECODE_CTAS")) target = std::atoll(env) > 0 ? std::atoll(env) : target;  // tuning
   int splits = static_cast<int>((target + ctas - 1) / ctas);
   const int max_by_len = (max_ctx + 255) / 256;  // at least 256 keys per split
   if (splits > max_by_len) splits = max_by_len;

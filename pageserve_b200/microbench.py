@@ -60,8 +60,11 @@ def _time(fn, iters, warmup=3, graph=True):
     return s.elapsed_time(e) / iters
 
 
-def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3, tiled=True):
-    from .quantization import LinearWorkspace, linear16, tile_int8_weight, w8a16_linear
+def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3, tiled=True, swiglu=False):
+    """swiglu: N = 2I rows (interleaved gate/up) through ps_linear_swiglu,
+    output (M, I) — the step's gate|up projection."""
+    from .quantization import (LinearWorkspace, QuantizedWeight, linear16, linear_swiglu, tile_int8_weight,
+                               w8a16_linear)
     dev = torch.device("cuda")
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -74,25 +77,30 @@ def bench_linear(M, N, K, iters=20, seed=0, bf16_weight=False, warmup=3, tiled=T
         tws = [tile_int8_weight(w) for w in ws] if tiled else [None] * copies
     scale = torch.empty(N, 1, device=dev).uniform_(1e-3, 1e-2, generator=g)
     x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
-    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(M, N // 2 if swiglu else N, device=dev, dtype=torch.bfloat16)
     wsp = LinearWorkspace()
     ctr = [0]
+    qws = [QuantizedWeight.from_quantized(w, scale, torch.bfloat16) for w in ws] if (swiglu and not bf16_weight) \
+        else None
 
     def f():
         w = ws[ctr[0] % copies]
         ctr[0] += 1
-        if bf16_weight:
+        if swiglu:
+            linear_swiglu(x, w if bf16_weight else qws[(ctr[0] - 1) % copies], out=out)
+        elif bf16_weight:
             linear16(x, w, out=out, workspace=wsp)
         else:
             w8a16_linear(x, w, scale, out=out, workspace=wsp, q_tiled=tws[(ctr[0] - 1) % copies])
     ms = _time(f, iters, warmup)
     hbm, tf = _peaks()
     flops = 2.0 * M * N * K
-    byts = wbytes + (0 if bf16_weight else 4 * N) + 2 * M * K + 2 * M * N
+    byts = wbytes + (0 if bf16_weight else 4 * N) + 2 * M * K + 2 * M * (N // 2 if swiglu else N)
     bound = "tensor" if flops / (tf * 1e12) > byts / (hbm * 1e9) else "hbm"
     ach_tf = flops / ms / 1e9
     ach_gb = byts / ms / 1e6
-    return {"case": "linear", "M": M, "N": N, "K": K, "weight": "bf16" if bf16_weight else "int8",
+    return {"case": "linear_swiglu" if swiglu else "linear", "M": M, "N": N, "K": K,
+            "weight": "bf16" if bf16_weight else "int8",
             "layout": "tiled" if (tiled and not bf16_weight) else "row-major", "us": ms * 1e3,
             "tflops": ach_tf, "gbs": ach_gb, "bound": bound,
             "frac": (ach_tf / tf) if bound == "tensor" else (ach_gb / hbm),
@@ -238,6 +246,7 @@ def main(argv=None):
     ap.add_argument("--K", type=int, default=2048)
     ap.add_argument("--bf16-weight", action="store_true")
     ap.add_argument("--row-major", action="store_true", help="int8 weight row-major (2D TMA) instead of pre-tiled")
+    ap.add_argument("--swiglu", action="store_true", help="gate|up linear with the SwiGLU epilogue (N = 2I)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
@@ -262,7 +271,7 @@ def main(argv=None):
         return 0
     if a.what == "linear":
         print(json.dumps(bench_linear(a.M, a.N, a.K, a.iters, bf16_weight=a.bf16_weight, warmup=a.warmup,
-                                      tiled=not a.row_major)))
+                                      tiled=not a.row_major, swiglu=a.swiglu)))
     elif a.what == "sweep":
         for n, k in SWEEP_NK:
             for m in SWEEP_M:
