@@ -59,7 +59,77 @@ struct AttnParams {
   int num_splits;
   int split_tokens;
   float scale_log2;
+  int num_seqs;
+  int balanced;     // decode TMA kernel: 1-D grid of equal key chunks (chunk size chosen on the device)
+  int* chunk_dev;   // balanced: the chunk size the attention kernel chose (read by the combine)
 };
+
+// Balanced decode split (device side): the smallest chunk size st (a
+// multiple of 64, >= kMinChunk) for which the (sequence, kv head, chunk)
+// items, Hkv * sum_b ceil(ctx_b / st), fit the grid (binary search over the
+// true context lengths, kept in registers for up to 256 sequences); items
+// are numbered sequence-major. Warp 0 finds item k's (b, h, c); b = -1 when
+// k is past the last item.
+constexpr int kMinChunk = 256;
+
+PS_DEVICE int seq_ctx(const AttnParams& p, int b) {
+  const int T_b = p.cu_q[b + 1] - p.cu_q[b];
+  if (T_b <= 0) return 0;
+  const int c = p.start_pos[b] + T_b;
+  return c < 0 ? 0 : (c > p.max_ctx ? p.max_ctx : c);
+}
+
+PS_DEVICE void balanced_item(const AttnParams& p, int k, int lane, int* b_out, int* h_out, int* c_out,
+                             int* st_out) {
+  const int cap = (p.max_ctx + 63) / 64 * 64;
+  long long st = cap;
+  if (p.num_seqs <= 256) {
+    int cr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cr[j] = lane + 32 * j < p.num_seqs ? seq_ctx(p, lane + 32 * j) : 0;
+    int lo = kMinChunk / 64, hi = cap / 64;
+    while (lo < hi) {
+      const int mid = (lo + hi) / 2;
+      const int cs = mid * 64;
+      int n = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) n += (cr[j] + cs - 1) / cs;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+      if (static_cast<long long>(n) * p.Hkv <= gridDim.x) hi = mid;
+      else lo = mid + 1;
+    }
+    st = static_cast<long long>(lo) * 64;
+  }
+  if (st > cap) st = cap;
+  int found_b = -1, found_local = 0;
+  long long running = 0;
+  for (int base = 0; base < p.num_seqs; base += 32) {
+    const int i = base + lane;
+    const int ctx = i < p.num_seqs ? seq_ctx(p, i) : 0;
+    const int n = p.Hkv * static_cast<int>((ctx + st - 1) / st);
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const long long lo = running + incl - n;
+    const bool mine = n > 0 && k >= lo && k < running + incl;
+    const unsigned hit = __ballot_sync(0xffffffffu, mine);
+    if (hit) {
+      const int src = __ffs(hit) - 1;
+      found_b = __shfl_sync(0xffffffffu, i, src);
+      found_local = __shfl_sync(0xffffffffu, static_cast<int>(k - lo), src);
+      break;
+    }
+    running += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  *b_out = found_b;
+  *h_out = found_local % p.Hkv;
+  *c_out = found_local / p.Hkv;
+  *st_out = static_cast<int>(st);
+}
 
 template <int D>
 struct Tile {
@@ -594,10 +664,34 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
   auto empty = [&](int s) { return bars + 8 * (kTmaStages + s); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kTmaStages * kTmaStageBytes + 8 * 2 * kTmaStages);
 
-  const int b = blockIdx.z;
-  const int h = blockIdx.y;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // which (sequence, kv head, key chunk) this CTA runs
+  __shared__ int s_item[4];
+  if (p.balanced) {
+    if (warp == 0) {
+      int ib, ih, ic, ist;
+      balanced_item(p, blockIdx.x, lane, &ib, &ih, &ic, &ist);
+      if (lane == 0) {
+        s_item[0] = ib;
+        s_item[1] = ih;
+        s_item[2] = ic;
+        s_item[3] = ist;
+        if (blockIdx.x == 0) *p.chunk_dev = ist;
+      }
+    }
+  } else if (threadIdx.x == 0) {
+    s_item[0] = blockIdx.z;
+    s_item[1] = blockIdx.y;
+    s_item[2] = blockIdx.x;
+    s_item[3] = p.split_tokens;
+  }
+  __syncthreads();
+  const int b = s_item[0];
+  const int h = s_item[1];
+  const int chunk = s_item[2];
+  const int chunk_keys = s_item[3];
+  if (b < 0) return;  // past the last item
   const int q0 = p.cu_q[b];
   const int T_b = p.cu_q[b + 1] - q0;
   const int sp = p.start_pos[b];
@@ -605,13 +699,14 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
   const int R = T_b * p.G;
   const int32_t* table = p.tables + static_cast<long long>(b) * p.max_blocks;
   if (T_b <= 0) return;
-  if (T_b > p.max_q_len || ctx > p.max_ctx || sp < 0 || ctx > p.max_blocks * p.block_size || R > 16) {
+  if (T_b > p.max_q_len || ctx > p.max_ctx || sp < 0 || ctx > p.max_blocks * p.block_size || R > 16 ||
+      chunk >= p.num_splits) {
     if (threadIdx.x == 0) record_error(p.status, kErrShape);
     return;
   }
-  const int kv_begin = blockIdx.x * p.split_tokens;
+  const int kv_begin = chunk * chunk_keys;
   if (kv_begin >= ctx) return;
-  const int kv_end = min(ctx, kv_begin + p.split_tokens);
+  const int kv_end = min(ctx, kv_begin + chunk_keys);
   const int ntiles = (kv_end - kv_begin + kTmaTile - 1) / kTmaTile;
 
   if (threadIdx.x == 0) {
@@ -770,7 +865,7 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
           *reinterpret_cast<uint32_t*>(dst + i2) = pack2<T>(acc[i2] * inv, acc[i2 + 1] * inv);
       } else {
         const long long prow =
-            (static_cast<long long>(b) * p.num_splits + blockIdx.x) * p.rows_max + t * p.Hq + h * p.G + g;
+            (static_cast<long long>(b) * p.num_splits + chunk) * p.rows_max + t * p.Hq + h * p.G + g;
         float* dst = p.o_part + prow * D + part * DP;
 #pragma unroll
         for (int i2 = 0; i2 < DP; i2 += 4)
@@ -795,7 +890,8 @@ __global__ void combine_kernel(const AttnParams p) {
   if (row >= T_b * p.Hq) return;
   // splits that saw this row's keys: positions 0 .. start_pos + t (causal)
   const int last_key = p.start_pos[b] + row / p.Hq;
-  const int nsplit = min(p.num_splits, last_key / p.split_tokens + 1);
+  const int st = p.balanced ? *p.chunk_dev : p.split_tokens;
+  const int nsplit = min(p.num_splits, last_key / st + 1);
   (void)ctx;
   const long long base = static_cast<long long>(b) * p.num_splits * p.rows_max + row;
   float mx = -FLT_MAX;
@@ -847,6 +943,16 @@ void plan_splits(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int 
     *num_splits = (max_ctx + st - 1) / st;
     return;
   }
+  if (D == 128) {
+    // the TMA decode kernel picks its chunk (>= kMinChunk keys) on the device
+    // from the actual context lengths; size partials for the smallest chunk
+    const int chunks = (max_ctx + kMinChunk - 1) / kMinChunk;
+    if (chunks > 1) {
+      *num_splits = chunks;
+      *split_tokens = kMinChunk;
+    }
+    return;
+  }
   const long long ctas = static_cast<long long>(num_seqs) * Hkv;
   // head_dim 128 runs the TMA kernel (2 CTAs per SM with a deep ring): about
   // 1.5 waves of long splits; the cp.async kernel wants many short ones.
@@ -867,7 +973,7 @@ size_t workspace_bytes_for(int num_seqs, int max_q_len, int max_ctx, int Hq, int
   plan_splits(num_seqs, max_q_len, max_ctx, Hq, Hkv, D, &ns, &st);
   if (ns <= 1) return 0;
   const size_t rows = static_cast<size_t>(num_seqs) * ns * max_q_len * Hq;
-  return rows * D * sizeof(float) + rows * sizeof(float) + 256;
+  return rows * D * sizeof(float) + rows * sizeof(float) + 256 + 16;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
@@ -915,7 +1021,13 @@ int launch_decode_tma(AttnParams& p, int num_seqs, int max_q_len, cudaStream_t s
     }
     attr = true;
   }
-  dim3 grid(p.num_splits, p.Hkv, num_seqs);
+  // With a split: a 1-D grid of two CTAs per SM (at least one per sequence x
+  // kv head) over equal key chunks, so the KV stream is spread evenly
+  // whatever the mix of context lengths.
+  p.balanced = p.num_splits > 1 ? 1 : 0;
+  const long long pairs = static_cast<long long>(num_seqs) * p.Hkv;
+  dim3 grid = p.balanced ? dim3(static_cast<unsigned>(pairs > 2 * 148 ? pairs : 2 * 148))
+                         : dim3(p.num_splits, p.Hkv, num_seqs);
   decode_tma_kernel<T><<<grid, 160, smem, s>>>(km, vm, p);
   ps_host::count_launch();
   int rc = ps_host::check_launch("paged_attention(decode, tma)");
@@ -1035,7 +1147,9 @@ int ps_paged_attention(void* out, const void* q, const void* k_cache, const void
     uintptr_t w = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
     p.o_part = reinterpret_cast<float*>(w);
     p.lse_part = p.o_part + rows * D;
+    p.chunk_dev = reinterpret_cast<int*>(p.lse_part + rows);
   }
+  p.num_seqs = num_seqs;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_BF16) {
     if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s);
@@ -1168,7 +1282,9 @@ extern "C" int ps_paged_attention_noalloc(void* out, const void* q, const void* 
     const size_t rows = static_cast<size_t>(num_seqs) * p.num_splits * p.rows_max;
     p.o_part = static_cast<float*>(scratch);  // the array is 256-byte aligned
     p.lse_part = p.o_part + rows * D;
+    p.chunk_dev = reinterpret_cast<int*>(p.lse_part + rows);
   }
+  p.num_seqs = num_seqs;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_BF16) {
     if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s);
