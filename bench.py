@@ -82,8 +82,12 @@ class Clocks:
             self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
+            # start timing only once the sampler writes (nvidia-smi takes ~0.1-1 s to come up)
+            t0 = time.time()
+            while time.time() - t0 < 3.0 and self.path.stat().st_size == 0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -118,7 +122,7 @@ class Clocks:
 
 # ------------------------------------------------------------- workload ----
 
-def build_workload(device, seed=0, tp=None, tp_comm="fused"):
+def build_workload(device, seed=0, tp=None, tp_comm="auto"):
     import numpy as np
     import torch
 
@@ -173,6 +177,28 @@ def time_events(fn, iters):
     ms = start.elapsed_time(end) / iters
     del g
     return ms
+
+
+# ncu summaries (profiles/) of the step's kernel classes: same kernel, same shape
+PROFILE_OF = {"gate_up": "linear_tc_gate_up_swiglu_M576.md", "down": "linear_tc_down_M576.md",
+              "qkv": "linear_tc_qkv_M576.md", "attn_decode": "decode_tma_cfg4.md"}
+
+
+def profile_traffic(kernel):
+    """dram__bytes_read.sum + dram__bytes_write.sum per launch of `kernel`
+    from its committed ncu summary (None when there is none)."""
+    name = PROFILE_OF.get(kernel)
+    if not name:
+        return None, None
+    path = ROOT / "profiles" / name
+    try:
+        for line in path.read_text().splitlines():
+            cells = [c.strip() for c in line.strip().strip("|").split("|")]
+            if len(cells) >= 2 and cells[0] == "traffic_bytes_per_launch":
+                return int(cells[1]), f"profiles/{name} (ncu dram__bytes_read.sum + dram__bytes_write.sum)"
+    except (OSError, ValueError):
+        pass
+    return None, None
 
 
 def kernel_breakdown(m, w, peaks):
@@ -247,7 +273,7 @@ def kernel_breakdown(m, w, peaks):
     return res
 
 
-def cpu_baseline_sample(layers_sampled=1, decode_seqs_sampled=4):
+def cpu_baseline_sample(layers_sampled=6, decode_seqs_sampled=8):
     """The reference algorithm on the host cores (oracle port of
     engine/model.py, per-sequence forward_step like engine/runner.py:65-79):
     a 1-layer 3B-shape model runs `decode_seqs_sampled` decode sequences at
@@ -293,8 +319,12 @@ def run_reference(args):
         return
     vals = []
     cb = None
-    for i in range(max(1, args.warmup) + max(1, args.steps)):
-        cb = cpu_baseline_sample()
+    # each step is a bounded sample (about 1 s per sampled layer) sized so the
+    # whole run stays within a few minutes
+    n = max(1, args.warmup) + max(1, args.steps)
+    layers = max(1, min(6, int(150 / n)))
+    for i in range(n):
+        cb = cpu_baseline_sample(layers_sampled=layers, decode_seqs_sampled=4)
         if i >= max(1, args.warmup):
             vals.append(cb["value"])
     v = statistics.median(vals)
@@ -388,14 +418,16 @@ def run_gpu(args):
     d = kb[dom]
     tensor_bound = dom in ("qkv", "o_proj", "gate_up", "down") and d["flops"] / peaks["bf16_tflops"] / 1e12 > \
         d["bytes"] / peaks["hbm_gbs"] / 1e9
+    traffic, traffic_src = profile_traffic(dom)
     if tensor_bound:
         roof = {"kernel": dom, "bound": "tensor", "achieved": d["tflops"], "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": d["tflops"] / peaks["bf16_tflops"], "traffic": None,
-                "algorithmic_per_launch": d["flops"], "peak_source": peaks["source"] + " (burst)"}
+                "unit": "TFLOP/s", "frac": d["tflops"] / peaks["bf16_tflops"], "traffic": traffic,
+                "algorithmic_per_launch": d["flops"], "algorithmic_bytes_per_launch": d["bytes"],
+                "peak_source": peaks["source"] + " (burst)", "traffic_source": traffic_src}
     else:
         roof = {"kernel": dom, "bound": "hbm", "achieved": d["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": d["gbs"] / peaks["hbm_gbs"], "traffic": None, "algorithmic_per_launch": d["bytes"],
-                "peak_source": peaks["source"]}
+                "frac": d["gbs"] / peaks["hbm_gbs"], "traffic": traffic, "algorithmic_per_launch": d["bytes"],
+                "peak_source": peaks["source"], "traffic_source": traffic_src}
     cpu = cpu_baseline_sample() if (not args.no_cpu_baseline and world == 1) else None
     clocks = clk.summary()
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -405,7 +437,7 @@ def run_gpu(args):
             "config": _config({"parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
                                else "single GPU",
                                **({"tp_allreduce": "fused peer-memory push (o_proj/down -> next RMSNorm)"
-                                   if args.tp_comm == "fused" else "NCCL all_reduce"} if tp else {})}),
+                                   if m.tp_comm == "fused" else "NCCL all_reduce"} if tp else {})}),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": g.h2d_bytes, "d2h_bytes_per_step": g.d2h_bytes,
                     "api": "StepGraph.run (host ids/metadata in, host next tokens out)"},
             "gpu_launches": launches, "launches_per_step": g.launches_per_replay,
@@ -432,13 +464,13 @@ def _finish(g, m, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="pageserve_b200", choices=["pageserve_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-breakdown", action="store_true", help="skip the per-kernel timing (for profiling runs)")
     ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
-    ap.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
+    ap.add_argument("--tp-comm", default="auto", choices=["auto", "fused", "nccl"],
                     help="N>1 tensor parallelism: row-parallel reduction transport")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -247,6 +247,9 @@ def main(argv=None):
     ap.add_argument("--bf16-weight", action="store_true")
     ap.add_argument("--row-major", action="store_true", help="int8 weight row-major (2D TMA) instead of pre-tiled")
     ap.add_argument("--swiglu", action="store_true", help="gate|up linear with the SwiGLU epilogue (N = 2I)")
+    ap.add_argument("--B", type=int, default=64, help="attn: decode sequences")
+    ap.add_argument("--lo", type=int, default=512, help="attn: shortest context")
+    ap.add_argument("--hi", type=int, default=4096, help="attn: longest context")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
@@ -279,7 +282,7 @@ def main(argv=None):
     elif a.what == "prefill":
         print(json.dumps(bench_attn_prefill(iters=a.iters, warmup=a.warmup)))
     else:
-        print(json.dumps(bench_attn(iters=a.iters, warmup=a.warmup)))
+        print(json.dumps(bench_attn(B=a.B, lo=a.lo, hi=a.hi, iters=a.iters, warmup=a.warmup)))
     from . import _lib
     _lib.raise_on_device_error()
     return 0

@@ -172,15 +172,18 @@ class PagedCausalLM:
 
     @classmethod
     def from_state_dict(cls, state_dict: dict, shape, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
-                        quantize: bool = True, max_position: int | None = None, tp=None, tp_comm: str = "fused",
+                        quantize: bool = True, max_position: int | None = None, tp=None, tp_comm: str = "auto",
                         tp_max_tokens: int = 4096) -> "PagedCausalLM":
         """Build from an HF-named state dict (numpy or torch tensors) and a
         ``synthetic.Qwen2Shape`` (the seeded random-init checkpoints). With
         ``tp`` (a ``tensor_parallel.TPGroup``) this rank loads only its
         Megatron shard (engine/tensor_parallel.py). ``tp_comm`` picks the
         row-parallel reduction: "fused" (peer-memory push from the linear into
-        the next RMSNorm, at most ``tp_max_tokens`` tokens per step) or "nccl"
-        (torch.distributed all_reduce, the reference's collective)."""
+        the next RMSNorm, at most ``tp_max_tokens`` tokens per step), "nccl"
+        (torch.distributed all_reduce, the reference's collective) or "auto"
+        (fused at 2 ranks, where it measured faster; NCCL above, where every
+        rank pushing its whole output to every peer moves W times the data of
+        a reduce-scatter + all-gather)."""
         cfg = SimpleNamespace(num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
                               hidden_size=shape.hidden, head_dim=shape.head_dim, rms_norm_eps=shape.rms_eps,
                               rope_theta=shape.rope_theta, rope_parameters=None,
@@ -191,7 +194,7 @@ class PagedCausalLM:
         obj._init(cfg, state_dict, device, dtype, quantize, shape.rope_theta, tp, tp_comm, tp_max_tokens)
         return obj
 
-    def _init(self, config, sd, device, dtype, quantize, theta, tp=None, tp_comm="fused", tp_max_tokens=4096):
+    def _init(self, config, sd, device, dtype, quantize, theta, tp=None, tp_comm="auto", tp_max_tokens=4096):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback)")
@@ -326,8 +329,11 @@ class PagedCausalLM:
                                                             self.device)
         self.attn_ws = AttentionWorkspace()
         self.lin_ws = LinearWorkspace()
-        if tp_comm not in ("fused", "nccl"):
-            raise ValueError(f"tp_comm must be 'fused' or 'nccl', not {tp_comm!r}")
+        if tp_comm not in ("fused", "nccl", "auto"):
+            raise ValueError(f"tp_comm must be 'fused', 'nccl' or 'auto', not {tp_comm!r}")
+        if tp_comm == "auto":
+            tp_comm = "fused" if (self.tp is not None and self.tp.world == 2) else "nccl"
+        self.tp_comm = tp_comm if self.tp is not None else None
         self.comm = None
         if self.tp is not None and tp_comm == "fused":
             from .comm import FusedAllReduce
