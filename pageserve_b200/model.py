@@ -181,9 +181,9 @@ class PagedCausalLM:
         row-parallel reduction: "fused" (peer-memory push from the linear into
         the next RMSNorm, at most ``tp_max_tokens`` tokens per step), "nccl"
         (torch.distributed all_reduce, the reference's collective) or "auto"
-        (fused at 2 ranks, where it measured faster; NCCL above, where every
-        rank pushing its whole output to every peer moves W times the data of
-        a reduce-scatter + all-gather)."""
+        (fused up to 4 ranks, where it measured faster than NCCL; NCCL at 8,
+        where every rank pushing its whole output to 7 peers moves several
+        times the data of a reduce-scatter + all-gather)."""
         cfg = SimpleNamespace(num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
                               hidden_size=shape.hidden, head_dim=shape.head_dim, rms_norm_eps=shape.rms_eps,
                               rope_theta=shape.rope_theta, rope_parameters=None,
@@ -332,7 +332,7 @@ class PagedCausalLM:
         if tp_comm not in ("fused", "nccl", "auto"):
             raise ValueError(f"tp_comm must be 'fused', 'nccl' or 'auto', not {tp_comm!r}")
         if tp_comm == "auto":
-            tp_comm = "fused" if (self.tp is not None and self.tp.world == 2) else "nccl"
+            tp_comm = "fused" if (self.tp is not None and self.tp.world <= 4) else "nccl"
         self.tp_comm = tp_comm if self.tp is not None else None
         self.comm = None
         if self.tp is not None and tp_comm == "fused":
