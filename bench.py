@@ -270,6 +270,22 @@ def kernel_breakdown(m, w, peaks):
     kv = N_DECODE * CTX * m.kv_heads_local * m.head_dim * 2 * 2
     byts = kv + 2 * 2 * N_DECODE * m.heads_local * m.head_dim + 4 * N_DECODE * (CTX // BLOCK)
     res["attn_decode"] = {"ms": ms, "gbs": byts / ms / 1e6, "bytes": byts}
+    # the 512-token prefill chunk at position 0 (causal), rotating over layer caches
+    pmeta = m.make_meta([PREFILL], [0], w["tables"][N_DECODE:])
+    qp = torch.randn(PREFILL, m.heads_local, m.head_dim, device=dev, dtype=torch.bfloat16)
+    ctr2 = [0]
+
+    def attp():
+        li = ctr2[0] % L
+        ctr2[0] += 1
+        paged_attention(qp, m.k_cache[li], m.v_cache[li], pmeta.block_tables, pmeta.cu_q, pmeta.start_pos, PREFILL,
+                        PREFILL, workspace=aws)
+    attp()
+    ms = time_events(attp, 2 * L)
+    flops = 4.0 * m.heads_local * m.head_dim * PREFILL * (PREFILL + 1) / 2
+    byts = 2 * PREFILL * m.kv_heads_local * m.head_dim * 2 + 2 * 2 * PREFILL * m.heads_local * m.head_dim
+    res["attn_prefill"] = {"ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "bytes": byts,
+                           "gbs": byts / ms / 1e6}
     return res
 
 
@@ -412,11 +428,12 @@ def run_gpu(args):
         _finish(g, m, world)
         return
     # dominant kernel: the largest per-step time share among the measured classes
-    per_step = {k: v["ms"] * (36 if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode") else 1)
+    per_step = {k: v["ms"] * (36 if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode", "attn_prefill") else 1)
                 for k, v in kb.items()}
     dom = max(per_step, key=per_step.get)
     d = kb[dom]
-    tensor_bound = dom in ("qkv", "o_proj", "gate_up", "down") and d["flops"] / peaks["bf16_tflops"] / 1e12 > \
+    tensor_bound = dom in ("qkv", "o_proj", "gate_up", "down", "attn_prefill") and \
+        d["flops"] / peaks["bf16_tflops"] / 1e12 > \
         d["bytes"] / peaks["hbm_gbs"] / 1e9
     traffic, traffic_src = profile_traffic(dom)
     if tensor_bound:

@@ -34,6 +34,12 @@ int linear_any(void* y, const void* x, const void* w, int wdtype, const float* s
     return PS_ERR_INVALID;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (wdtype == PS_I8 && M <= ps_host::mma_max_m() && dtype != PS_F32 && ps_host::aligned(resid, 2) &&
+      ps_host::aligned(bias, 2)) {
+    const int rc = ps_host::linear_mma(y, x, static_cast<const int8_t*>(w), false, scale, bias, resid, M, N, K, dtype,
+                                       false, s);
+    if (rc != PS_ERR_UNSUPPORTED) return rc;
+  }
   if (M > simt_max_m() && dtype != PS_F32) {
     const int rc = ps_host::linear_tc(y, x, w, wdtype, scale, bias, resid, M, N, K, dtype, ws, ws_bytes, s);
     if (rc != PS_ERR_UNSUPPORTED) return rc;
@@ -42,6 +48,17 @@ int linear_any(void* y, const void* x, const void* w, int wdtype, const float* s
 }
 
 }  // namespace
+
+namespace ps_host {
+int mma_max_m() {
+  static const int v = [] {
+    const char* e = std::getenv("PS_MMA_MAX_M");
+    const int m = e ? std::atoi(e) : kMmaDefaultMaxM;
+    return m < 0 ? 0 : (m > kMmaMaxM ? kMmaMaxM : m);
+  }();
+  return v;
+}
+}  // namespace ps_host
 
 extern "C" {
 
@@ -86,6 +103,11 @@ int ps_w8a16_linear_tiled(void* y, const void* x, const int8_t* q_tiled, const f
     ps_host::set_error("w8a16_linear_tiled: tensors must be 16-byte aligned and K a multiple of 16");
     return PS_ERR_INVALID;
   }
+  if (M <= ps_host::mma_max_m()) {
+    const int rc = ps_host::linear_mma(y, x, q_tiled, true, scale, bias, resid, M, N, K, dtype, false,
+                                       reinterpret_cast<cudaStream_t>(stream));
+    if (rc != PS_ERR_UNSUPPORTED) return rc;
+  }
   return ps_host::linear_tc(y, x, q_tiled, PS_I8, scale, bias, resid, M, N, K, dtype, ws, ws_bytes,
                             reinterpret_cast<cudaStream_t>(stream), q_tiled);
 }
@@ -113,6 +135,11 @@ int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_til
   const int rc = ps_host::push_targets(&pt, rank_bufs, world, rank, set, max_tokens, N, 2);
   if (rc != PS_OK) return rc;
   const int8_t* wt = int8 ? w_tiled : nullptr;
+  if (int8 && M <= ps_host::mma_max_m()) {
+    const int r1 = ps_host::linear_mma(nullptr, x, w_tiled, true, scale, nullptr, nullptr, M, N, K, dtype, false,
+                                       reinterpret_cast<cudaStream_t>(stream), &pt);
+    if (r1 != PS_ERR_UNSUPPORTED) return r1;
+  }
   const int r2 = ps_host::linear_tc(nullptr, x, int8 ? static_cast<const void*>(w_tiled) : w, wdtype, scale, nullptr,
                                     nullptr, M, N, K, dtype, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream),
                                     wt, &pt);
@@ -136,6 +163,11 @@ int ps_linear_swiglu(void* y, const void* x, const void* w, int wdtype, const in
       !ps_host::aligned(w, 16) || !ps_host::aligned(w_tiled, 16) || !ps_host::aligned(scale, 16)) {
     ps_host::set_error("linear_swiglu: 2*intermediate must be a multiple of 16, K of 16, tensors 16-byte aligned");
     return PS_ERR_INVALID;
+  }
+  if (int8 && M <= ps_host::mma_max_m()) {
+    const int r1 = ps_host::linear_mma(y, x, w_tiled, true, scale, nullptr, nullptr, M, N2, K, dtype, true,
+                                       reinterpret_cast<cudaStream_t>(stream));
+    if (r1 != PS_ERR_UNSUPPORTED) return r1;
   }
   const int rc = ps_host::linear_tc(y, x, int8 ? static_cast<const void*>(w_tiled) : w, wdtype, scale, nullptr,
                                     nullptr, M, N2, K, dtype, nullptr, 0, reinterpret_cast<cudaStream_t>(stream),

@@ -930,7 +930,9 @@ void plan_splits(int num_seqs, int max_q_len, int max_ctx, int Hq, int Hkv, int 
     // SM (one warp per SM sub-partition leaves every mma.sync stall exposed),
     // as long as the (o, lse) partials fit the workspace cap.
     const long long base = static_cast<long long>((max_q_len * G + 63) / 64) * Hkv * num_seqs;
-    int splits = static_cast<int>((3LL * 148 + base - 1) / base);
+    long long target = 3LL * 148;
+    if (const char* env = std::getenv("PS_ATTN_PREFILL_CTAS")) target = std::atoll(env) > 0 ? std::atoll(env) : target;  // tuning
+    int splits = static_cast<int>((target + base - 1) / base);
     const int max_by_len = (max_ctx + 127) / 128;
     if (splits > max_by_len) splits = max_by_len;
     while (splits > 1 &&
