@@ -775,19 +775,33 @@ Plan plan(int M, int N, int K, bool int8) {
   const int mt = (M + 255) / 256;
   pl.bm = snap_bm((((M + mt - 1) / mt) + 15) / 16 * 16);
   pl.k_tiles = (K + kBK - 1) / kBK;
-  const int m_tiles = (M + pl.bm - 1) / pl.bm;
+  int m_tiles = (M + pl.bm - 1) / pl.bm;
   const int nt1 = (N + 127) / 128, nt2 = (N + 255) / 256;
   int splits = 1;
   if (pl.bm >= 128) {
+    // Narrow outputs with few token tiles (M up to ~256) would leave most SMs
+    // idle even after the K split: 128-token tiles double the tile count.
+    const int m128 = (M + 127) / 128;
     if (N >= 8192) {
       pl.nsub = 2;
     } else if (K >= 8192) {
       pl.nsub = 2;
+      if (pl.bm > 128 && nt2 * m_tiles * 8 < 100) {
+        pl.bm = 128;
+        m_tiles = m128;
+      }
       splits = 148 / (nt2 * m_tiles);
       if (splits > 8) splits = 8;
     } else {
       pl.nsub = 1;
       splits = 2;
+      if (pl.bm > 128 && nt1 * m_tiles * 2 < 74) {
+        pl.bm = 128;
+        m_tiles = m128;
+        splits = 148 / (nt1 * m_tiles);
+        if (splits > 4) splits = 4;
+        if (splits < 1) splits = 1;
+      }
     }
   } else {
     pl.nsub = (nt1 * m_tiles > 148 && nt2 * m_tiles <= 148) ? 2 : 1;
