@@ -2,6 +2,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -47,6 +48,14 @@ int* status_word(int tu) {
     g_status[dev] = p;
   }
   return g_status[dev] + tu;
+}
+
+bool pdl_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("PS_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return v;
 }
 
 }  // namespace ps_host

@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(T* __restrict__ 
                                                                 const T* __restrict__ w, float eps, int M, int H,
                                                                 void* buf, int W, int set, long long slot_elems,
                                                                 int* status) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   __shared__ float red[8];
   unsigned* flag = ctrl_flag(buf, set);
@@ -288,7 +290,7 @@ PS_API int ps_allreduce_rmsnorm(void* y, void* x, const void* weight, float eps,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int* st = ps_host::status_word(PS_TU_COMM);
 #define PS_ARN(T, MV, NORM)                                                                                   \
-  allreduce_rmsnorm_kernel<T, MV, NORM><<<M, 256, 0, s>>>(static_cast<T*>(y), static_cast<T*>(x),            \
+  ps_host::launch(allreduce_rmsnorm_kernel<T, MV, NORM>, M, 256, 0, s, static_cast<T*>(y), static_cast<T*>(x),            \
                                                           static_cast<const T*>(weight), eps, M, H, buf, world, \
                                                           set, slot, st)
 #define PS_ARN_N(T, MV) \

@@ -131,6 +131,15 @@ PS_DEVICE float warp_max(float v) {
 // error ~1e-6, far below the bf16/f16 output rounding; 0 for g -> -inf).
 PS_DEVICE float silu_mul_f32(float g, float u) { return __fdividef(g, 1.f + __expf(-g)) * u; }
 
+// Programmatic dependent launch (kernels launched through ps_host::launch):
+// the next kernel in the stream may start while this one finishes. A kernel
+// calls pdl_wait() before it reads anything an earlier kernel writes and
+// before any global write (it returns once the previous grid has completed
+// and its writes are visible), and pdl_trigger() to let the next kernel begin
+// launching. Without the launch attribute both are no-ops.
+PS_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+PS_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 PS_DEVICE void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
@@ -139,6 +148,23 @@ PS_DEVICE void record_error(int* status, int code) {
 
 // Host-side helpers shared by the .cu files.
 namespace ps_host {
+bool pdl_enabled();  // programmatic dependent launch on (PS_PDL=0 turns it off)
+// Launch `kern` with the programmatic-dependent-launch attribute; `kern` must
+// call ps::pdl_wait() before touching memory earlier kernels write.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
 void set_error(const char* fmt, ...);
 int check_launch(const char* what);
 void count_launch(int n = 1);

@@ -41,6 +41,8 @@ __global__ void slot_mapping_kernel(int32_t* __restrict__ positions, int32_t* __
                                     const int32_t* __restrict__ tables, int max_blocks,
                                     const int32_t* __restrict__ cu_q, const int32_t* __restrict__ start_pos,
                                     int num_seqs, int total_tokens, int num_blocks, int block_size, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= total_tokens) return;
   // sequence of token t: last b with cu_q[b] <= t
@@ -74,6 +76,8 @@ __global__ void rope_qkv_kernel(T* __restrict__ q_out, T* __restrict__ k_cache, 
                                 const int32_t* __restrict__ slots, const float* __restrict__ cos_tab,
                                 const float* __restrict__ sin_tab, int max_pos, int num_tokens, int Hq, int Hkv,
                                 int D, int num_slots, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int half = D / 2;
   const int chunks = half / 8;
   const int heads = Hq + 2 * Hkv;
@@ -228,8 +232,8 @@ int ps_build_slot_mapping(int32_t* positions, int32_t* slots, const int32_t* tab
   }
   if (total_tokens == 0) return PS_OK;
   const int threads = 256;
-  slot_mapping_kernel<<<(total_tokens + threads - 1) / threads, threads, 0,
-                        reinterpret_cast<cudaStream_t>(stream)>>>(positions, slots, tables, max_blocks, cu_q,
+  ps_host::launch(slot_mapping_kernel, (total_tokens + threads - 1) / threads, threads, 0,
+                        reinterpret_cast<cudaStream_t>(stream), positions, slots, tables, max_blocks, cu_q,
                                                                   start_pos, num_seqs, total_tokens, num_blocks,
                                                                   block_size, ps_host::status_word(PS_TU_KV));
   ps_host::count_launch();
@@ -254,12 +258,12 @@ int ps_rope_qkv_write_kv(void* q_out, void* k_cache, void* v_cache, const void* 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int* status = ps_host::status_word(PS_TU_KV);
   if (dtype == PS_BF16) {
-    rope_qkv_kernel<__nv_bfloat16><<<grid_for(work, threads), threads, 0, s>>>(
+    ps_host::launch(rope_qkv_kernel<__nv_bfloat16>, grid_for(work, threads), threads, 0, s, 
         static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
         static_cast<__nv_bfloat16*>(v_cache), static_cast<const __nv_bfloat16*>(qkv), positions, slots, rope_cos,
         rope_sin, max_pos, T, Hq, Hkv, D, num_slots, status);
   } else if (dtype == PS_F16) {
-    rope_qkv_kernel<__half><<<grid_for(work, threads), threads, 0, s>>>(
+    ps_host::launch(rope_qkv_kernel<__half>, grid_for(work, threads), threads, 0, s, 
         static_cast<__half*>(q_out), static_cast<__half*>(k_cache), static_cast<__half*>(v_cache),
         static_cast<const __half*>(qkv), positions, slots, rope_cos, rope_sin, max_pos, T, Hq, Hkv, D, num_slots,
         status);

@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(W * 32) linear_mma_kernel(
     const float* __restrict__ scale, const T* __restrict__ bias, const T* __restrict__ resid, int M, int N, int K,
     int swiglu, const PushTargets push) {
   __shared__ float red[W][16][NT * 8 + 1];
+  pdl_trigger();
+  bool waited = false;  // the first weight loads go out before waiting for the previous kernel
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int k_tiles = (K + kKT - 1) / kKT;
@@ -91,6 +93,10 @@ __global__ void __launch_bounds__(W * 32) linear_mma_kernel(
     uint4 qa[kDepth], qb[kDepth];
 #pragma unroll
     for (int i = 0; i < kDepth; ++i) load_w(warp + i * W, qa[i], qb[i]);
+    if (!waited) {
+      pdl_wait();  // activations and outputs belong to earlier kernels
+      waited = true;
+    }
     for (int kt0 = warp; kt0 < k_tiles; kt0 += kDepth * W) {
 #pragma unroll
       for (int i = 0; i < kDepth; ++i) {
@@ -170,6 +176,7 @@ __global__ void __launch_bounds__(W * 32) linear_mma_kernel(
     }
     __syncthreads();  // red is reused by the next row group
   }
+  if (!waited) pdl_wait();
   if (push.world > 0) push_arrive(push);
 }
 
@@ -196,7 +203,7 @@ int launch_w(void* y, const void* x, const int8_t* q, bool tiled, const float* s
 #define PS_MMA_LAUNCH(NT)                                                                                         \
   {                                                                                                               \
     auto kern = linear_mma_kernel<T, NT, W, (W > 8 ? 4 : 2)>;                                                     \
-    kern<<<grid_for(kern), W * 32, 0, s>>>(static_cast<T*>(y), static_cast<const T*>(x), q, tiled ? 1 : 0, scale, \
+    ps_host::launch(kern, grid_for(kern), W * 32, 0, s, static_cast<T*>(y), static_cast<const T*>(x), q, tiled ? 1 : 0, scale, \
                                            static_cast<const T*>(bias), static_cast<const T*>(resid), M, N, K,    \
                                            swiglu ? 1 : 0, pt);                                                   \
   }

@@ -375,6 +375,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   PS_TC_TRACE(1, threadIdx.x == 0);
+  // Programmatic dependent launch: the weight producer starts streaming the
+  // (never written) weights while the previous kernel finishes; every other
+  // role waits for it before reading activations / residuals or writing.
+  pdl_trigger();
+  if (warp != 0) pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------- weight producer --
@@ -895,13 +900,22 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kBytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = pl.splits;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (ps_host::pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (pl.splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = pl.splits;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pl.splits > 1 ? 1 : 0;
+  cfg.numAttrs = na;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wm, xm, p, om);
   if (e != cudaSuccess) {
     ps_host::set_error("linear_tc: launch failed: %s", cudaGetErrorString(e));

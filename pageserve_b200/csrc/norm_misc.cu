@@ -17,6 +17,8 @@ template <typename T, int MAXV>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(T* __restrict__ y, T* __restrict__ resid_out,
                                                                const T* __restrict__ x, const T* __restrict__ resid,
                                                                const T* __restrict__ w, float eps, int H) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int row = blockIdx.x;
   const int nvec = H / VEC;
@@ -80,6 +82,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(T* __restrict__ y
 template <typename T>
 __global__ void embedding_kernel(T* __restrict__ out, const int64_t* __restrict__ ids, const T* __restrict__ table,
                                  int H, int vocab, int* status) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int t = blockIdx.x;
   const long long id = ids[t];
@@ -107,6 +111,8 @@ PS_DEVICE void argmax_merge(float& best, int& bidx, float ob, int oi) {
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(int32_t* __restrict__ out, const T* __restrict__ logits,
                                                       int V, int ld) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int row = blockIdx.x;
   const T* lr = logits + static_cast<long long>(row) * ld;
@@ -238,7 +244,7 @@ int ps_rmsnorm(void* y, void* resid_out, const void* x, const void* resid, const
   const int per_thread = (nvec + kNormThreads - 1) / kNormThreads;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 #define PS_NORM(T, MV)                                                                                     \
-  rmsnorm_kernel<T, MV><<<M, kNormThreads, 0, s>>>(static_cast<T*>(y), static_cast<T*>(resid_out),        \
+  ps_host::launch(rmsnorm_kernel<T, MV>, M, kNormThreads, 0, s, static_cast<T*>(y), static_cast<T*>(resid_out),        \
                                                     static_cast<const T*>(x), static_cast<const T*>(resid), \
                                                     static_cast<const T*>(w), eps, H)
 #define PS_NORM_T(T)            \
@@ -273,9 +279,9 @@ int ps_embedding(void* out, const int64_t* ids, const void* table, int T, int H,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int* st = ps_host::status_word(PS_TU_MISC);
   switch (dtype) {
-    case PS_F32: embedding_kernel<float><<<T, 128, 0, s>>>(static_cast<float*>(out), ids, static_cast<const float*>(table), H, vocab, st); break;
-    case PS_BF16: embedding_kernel<__nv_bfloat16><<<T, 128, 0, s>>>(static_cast<__nv_bfloat16*>(out), ids, static_cast<const __nv_bfloat16*>(table), H, vocab, st); break;
-    case PS_F16: embedding_kernel<__half><<<T, 128, 0, s>>>(static_cast<__half*>(out), ids, static_cast<const __half*>(table), H, vocab, st); break;
+    case PS_F32: ps_host::launch(embedding_kernel<float>, T, 128, 0, s, static_cast<float*>(out), ids, static_cast<const float*>(table), H, vocab, st); break;
+    case PS_BF16: ps_host::launch(embedding_kernel<__nv_bfloat16>, T, 128, 0, s, static_cast<__nv_bfloat16*>(out), ids, static_cast<const __nv_bfloat16*>(table), H, vocab, st); break;
+    case PS_F16: ps_host::launch(embedding_kernel<__half>, T, 128, 0, s, static_cast<__half*>(out), ids, static_cast<const __half*>(table), H, vocab, st); break;
     default: ps_host::set_error("embedding: unsupported dtype"); return PS_ERR_UNSUPPORTED;
   }
   ps_host::count_launch();
@@ -290,9 +296,9 @@ int ps_argmax(int32_t* out, const void* logits, int M, int V, int ld, int dtype,
   if (M == 0) return PS_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case PS_F32: argmax_kernel<float><<<M, 1024, 0, s>>>(out, static_cast<const float*>(logits), V, ld); break;
-    case PS_BF16: argmax_kernel<__nv_bfloat16><<<M, 1024, 0, s>>>(out, static_cast<const __nv_bfloat16*>(logits), V, ld); break;
-    case PS_F16: argmax_kernel<__half><<<M, 1024, 0, s>>>(out, static_cast<const __half*>(logits), V, ld); break;
+    case PS_F32: ps_host::launch(argmax_kernel<float>, M, 1024, 0, s, out, static_cast<const float*>(logits), V, ld); break;
+    case PS_BF16: ps_host::launch(argmax_kernel<__nv_bfloat16>, M, 1024, 0, s, out, static_cast<const __nv_bfloat16*>(logits), V, ld); break;
+    case PS_F16: ps_host::launch(argmax_kernel<__half>, M, 1024, 0, s, out, static_cast<const __half*>(logits), V, ld); break;
     default: ps_host::set_error("argmax: unsupported dtype"); return PS_ERR_UNSUPPORTED;
   }
   ps_host::count_launch();

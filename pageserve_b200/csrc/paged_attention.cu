@@ -392,6 +392,8 @@ PS_DEVICE void load_q(uint32_t (*qa)[4], const AttnParams& p, int q0, int h, int
 
 template <typename T, int D, bool DECODE>
 __global__ void __launch_bounds__(kThreads) paged_attention_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) unsigned char smem[];
   const int b = blockIdx.z;
   const int h = blockIdx.y;
@@ -654,6 +656,8 @@ template <typename T>
 __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__ CUtensorMap kmap,
                                                          const __grid_constant__ CUtensorMap vmap,
                                                          const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = 128;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -880,6 +884,8 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
 // Merge split partials: one warp per (sequence, chunk token, q head) row.
 template <typename T, int D>
 __global__ void combine_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y;
   const int q0 = p.cu_q[b];
   const int T_b = p.cu_q[b + 1] - q0;
@@ -1030,13 +1036,13 @@ int launch_decode_tma(AttnParams& p, int num_seqs, int max_q_len, cudaStream_t s
   const long long pairs = static_cast<long long>(num_seqs) * p.Hkv;
   dim3 grid = p.balanced ? dim3(static_cast<unsigned>(pairs > 2 * 148 ? pairs : 2 * 148))
                          : dim3(p.num_splits, p.Hkv, num_seqs);
-  decode_tma_kernel<T><<<grid, 160, smem, s>>>(km, vm, p);
+  ps_host::launch(decode_tma_kernel<T>, grid, 160, smem, s, km, vm, p);
   ps_host::count_launch();
   int rc = ps_host::check_launch("paged_attention(decode, tma)");
   if (rc != PS_OK || p.num_splits == 1) return rc;
   const int rows = max_q_len * p.Hq;
   dim3 cgrid((rows + 3) / 4, num_seqs);
-  combine_kernel<T, 128><<<cgrid, 128, 0, s>>>(p);
+  ps_host::launch(combine_kernel<T, 128>, cgrid, 128, 0, s, p);
   ps_host::count_launch();
   return ps_host::check_launch("paged_attention(combine)");
 }
@@ -1057,26 +1063,26 @@ int launch(AttnParams& p, int num_seqs, int max_q_len, int max_ctx, cudaStream_t
     auto kern = paged_attention_kernel<T, D, true>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 grid(p.num_splits, p.Hkv, num_seqs);
-    kern<<<grid, kThreads, smem, s>>>(p);
+    ps_host::launch(kern, grid, kThreads, smem, s, p);
     ps_host::count_launch();
     int rc = ps_host::check_launch("paged_attention(decode)");
     if (rc != PS_OK || p.num_splits == 1) return rc;
     const int rows = max_q_len * p.Hq;
     dim3 cgrid((rows + 3) / 4, num_seqs);
-    combine_kernel<T, D><<<cgrid, 128, 0, s>>>(p);
+    ps_host::launch(combine_kernel<T, D>, cgrid, 128, 0, s, p);
     ps_host::count_launch();
     return ps_host::check_launch("paged_attention(combine)");
   }
   auto kern = paged_attention_kernel<T, D, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid(((max_q_len * p.G + 63) / 64) * p.num_splits, p.Hkv, num_seqs);
-  kern<<<grid, kThreads, smem, s>>>(p);
+  ps_host::launch(kern, grid, kThreads, smem, s, p);
   ps_host::count_launch();
   int rc = ps_host::check_launch("paged_attention(prefill)");
   if (rc != PS_OK || p.num_splits == 1) return rc;
   const int rows = max_q_len * p.Hq;
   dim3 cgrid((rows + 3) / 4, num_seqs);
-  combine_kernel<T, D><<<cgrid, 128, 0, s>>>(p);
+  ps_host::launch(combine_kernel<T, D>, cgrid, 128, 0, s, p);
   ps_host::count_launch();
   return ps_host::check_launch("paged_attention(prefill combine)");
 }
