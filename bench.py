@@ -55,8 +55,10 @@ def _peaks():
 
 
 def _config(extra=None):
-    c = {"workload": "BASELINE config 4: Qwen2.5-3B-shape int8 mixed step, 64 decode seqs @ctx 2048 "
-                     "+ one 512-token prefill chunk, block 16",
+    c = {"workload": ("BASELINE config 4: Qwen2.5-3B-shape int8 mixed step, 64 decode seqs @ctx 2048 "
+                      f"+ one {PREFILL}-token prefill chunk, block 16") if PREFILL else
+                     "Qwen2.5-3B-shape int8 decode-only step (config 4 without its prefill chunk): 64 decode seqs "
+                     "@ctx 2048, block 16",
          "model": "qwen2.5-3b-shape (random init)", "layers": 36, "global_batch": N_DECODE,
          "prefill_tokens_per_step": PREFILL, "seq_len": CTX, "kv_dtype": "bf16", "weights": "int8 per-channel",
          "l2": "inputs larger than L2 (~8 GB streamed per step)"}
@@ -149,9 +151,10 @@ def build_workload(device, seed=0, tp=None, tp_comm="auto"):
     for _ in range(N_DECODE):
         tables.append(perm[at:at + nblk_dec].tolist())
         at += nblk_dec
-    tables.append(perm[at:at + nblk_pre].tolist())
-    q_lens = [1] * N_DECODE + [PREFILL]
-    start_pos = [CTX - 1] * N_DECODE + [0]
+    if PREFILL:
+        tables.append(perm[at:at + nblk_pre].tolist())
+    q_lens = [1] * N_DECODE + ([PREFILL] if PREFILL else [])
+    start_pos = [CTX - 1] * N_DECODE + ([0] if PREFILL else [])
     ids = rng.integers(0, shape.vocab, size=N_DECODE + PREFILL).astype(np.int64)
     return m, dict(q_lens=q_lens, start_pos=start_pos, tables=tables, ids=ids, shape=shape)
 
@@ -188,7 +191,7 @@ def profile_traffic(kernel):
     """dram__bytes_read.sum + dram__bytes_write.sum per launch of `kernel`
     from its committed ncu summary (None when there is none)."""
     name = PROFILE_OF.get(kernel)
-    if not name:
+    if not name or PREFILL != 512:  # the captures are of the config-4 shapes (576 tokens)
         return None, None
     path = ROOT / "profiles" / name
     try:
@@ -270,7 +273,9 @@ def kernel_breakdown(m, w, peaks):
     kv = N_DECODE * CTX * m.kv_heads_local * m.head_dim * 2 * 2
     byts = kv + 2 * 2 * N_DECODE * m.heads_local * m.head_dim + 4 * N_DECODE * (CTX // BLOCK)
     res["attn_decode"] = {"ms": ms, "gbs": byts / ms / 1e6, "bytes": byts}
-    # the 512-token prefill chunk at position 0 (causal), rotating over layer caches
+    if not PREFILL:
+        return res
+    # the prefill chunk at position 0 (causal), rotating over layer caches
     pmeta = m.make_meta([PREFILL], [0], w["tables"][N_DECODE:])
     qp = torch.randn(PREFILL, m.heads_local, m.head_dim, device=dev, dtype=torch.bfloat16)
     ctr2 = [0]
@@ -316,14 +321,16 @@ def cpu_baseline_sample(layers_sampled=6, decode_seqs_sampled=8):
     t0 = time.perf_counter()
     for i in range(decode_seqs_sampled):
         o.forward_step([int(rng.integers(0, shape.vocab))], tabs[i], CTX - 1, timings=t_dec)
-    o.forward_step(rng.integers(0, shape.vocab, size=PREFILL), tabs[-1], 0, timings=t_pre)
+    if PREFILL:
+        o.forward_step(rng.integers(0, shape.vocab, size=PREFILL), tabs[-1], 0, timings=t_pre)
     wall = time.perf_counter() - t0
     per_dec = (t_dec["layers"] / layers_sampled * 36 + t_dec["head"]) / decode_seqs_sampled
-    step = N_DECODE * per_dec + (t_pre["layers"] / layers_sampled * 36 + t_pre["head"])
+    step = N_DECODE * per_dec + ((t_pre["layers"] / layers_sampled * 36 + t_pre["head"]) if PREFILL else 0.0)
     return {"value": N_DECODE / step, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
             "sample": (f"oracle port of the reference step (numpy/BLAS, per-sequence forward_step); "
-                       f"{layers_sampled} of 36 layers, {decode_seqs_sampled} of 64 decode seqs + the 512-token "
-                       f"chunk, scaled to the full step; sample wall {wall:.1f} s"),
+                       f"{layers_sampled} of 36 layers, {decode_seqs_sampled} of 64 decode seqs"
+                       + (f" + the {PREFILL}-token chunk" if PREFILL else "")
+                       + f", scaled to the full step; sample wall {wall:.1f} s"),
             "step_s": step}
 
 
@@ -487,9 +494,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-breakdown", action="store_true", help="skip the per-kernel timing (for profiling runs)")
     ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
+    ap.add_argument("--prefill", type=int, default=None,
+                    help="prefill chunk tokens per step (default 512 = BASELINE config 4; 0 = decode-only step)")
     ap.add_argument("--tp-comm", default="auto", choices=["auto", "fused", "nccl"],
                     help="N>1 tensor parallelism: row-parallel reduction transport")
     args = ap.parse_args()
+    global PREFILL
+    if args.prefill is not None:
+        PREFILL = max(0, args.prefill)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -19,9 +19,9 @@
 //   warp 2      activation producer: TMA of the bf16 tile (BM x 128 B,
 //               128B swizzle) into its ring
 //   warps 3..10 widen int8 -> bf16 (exact: |q| <= 127) straight into a
-//               2-deep ring of MMA A operands in tensor memory (tcgen05.st; one
+//               2..4-deep ring of MMA A operands in tensor memory (tcgen05.st; one
 //               weight row per lane, K packed two bf16 per column), running up
-//               to two k-tiles ahead of the MMA, which reads A from TMEM
+//               to that many k-tiles ahead of the MMA, which reads A from TMEM
 //               (tcgen05.mma ... [a_tmem]) and only the activations from
 //               shared memory; then they copy the accumulators from TMEM
 //               (tcgen05.ld 32x32b; warp w reads lane quarter w%4) into a
@@ -298,7 +298,12 @@ struct Cfg {
   static constexpr int kOffStage = kOffW;
   static constexpr int kOffBar = kOffX + kRX * kX;
   static constexpr int kBytes = kOffBar + 512 + 1024;
-  static constexpr int kTmemNeed = kAccCols + 2 * kACols;  // accumulators + two A stages
+  // widened-A stages in TMEM: as many as fit beside the accumulators (2..4);
+  // small token tiles get a deeper ring, which hides the widen -> MMA ->
+  // commit round trip when the MMAs are short
+  static constexpr int kATm = kInt8 ? ((512 - kAccCols) / kACols >= 4 ? 4 : ((512 - kAccCols) / kACols >= 3 ? 3 : 2))
+                                    : 2;
+  static constexpr int kTmemNeed = kAccCols + kATm * kACols;  // accumulators + the A stages
   static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 :
                                    (kTmemNeed <= 256 ? 256 : 512)));
   static_assert(kBytes <= 227 * 1024, "shared memory plan too large");
@@ -327,12 +332,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto w_empty = [&](int s) { return bars + 8 * (8 + s); };
   auto x_full = [&](int s) { return bars + 8 * (16 + s); };
   auto x_empty = [&](int s) { return bars + 8 * (24 + s); };
+  constexpr int AS = C::kATm;
   auto a_full = [&](int s) { return bars + 8 * (32 + s); };
-  auto a_empty = [&](int s) { return bars + 8 * (34 + s); };
-  const uint32_t acc_full = bars + 8 * 36;
-  const uint32_t res_full = bars + 8 * 37;   // residual tiles landed (TMA output path)
-  const uint32_t recv_full = bars + 8 * 38;  // split-K slices from the cluster peers landed
-  unsigned char* misc = gbase + C::kOffBar + 8 * 40;
+  auto a_empty = [&](int s) { return bars + 8 * (36 + s); };
+  const uint32_t acc_full = bars + 8 * 40;
+  const uint32_t res_full = bars + 8 * 41;   // residual tiles landed (TMA output path)
+  const uint32_t recv_full = bars + 8 * 42;  // split-K slices from the cluster peers landed
+  unsigned char* misc = gbase + C::kOffBar + 8 * 44;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 4);
 
@@ -355,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(x_full(s), 1);
       mbar_init(x_empty(s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < AS; ++s) {
       mbar_init(a_full(s), kDeqWarps);
       mbar_init(a_empty(s), 1);
     }
@@ -422,8 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = nkt > 0;
     for (int i = 0; i < nkt; ++i) {
       const int sx = i % RX;
-      const int sa = kInt8 ? (i & 1) : (i % RW);
-      ok = warp_wait(kInt8 ? a_full(sa) : w_full(sa), kInt8 ? ((i >> 1) & 1) : ((i / RW) & 1), abort_flag,
+      const int sa = kInt8 ? (i % AS) : (i % RW);
+      ok = warp_wait(kInt8 ? a_full(sa) : w_full(sa), kInt8 ? ((i / AS) & 1) : ((i / RW) & 1), abort_flag,
                      p.status);
       if (ok) ok = warp_wait(x_full(sx), (i / RX) & 1, abort_flag, p.status);
       if (!ok) break;
@@ -469,10 +475,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tcol0 = (NSUB == 2 ? sub * (kBK / 2) : h * (kBK / 4));
       for (int i = 0; i < nkt; ++i) {
         const int sw = i % RW;
-        const int sa = i & 1;
+        const int sa = i % AS;
         if (!warp_wait(w_full(sw), (i / RW) & 1, abort_flag, p.status)) break;
         PS_TC_TRACE(16 + (i & 255) * 8 + 5, t == 0);
-        if (i >= 2 && !warp_wait(a_empty(sa), ((i >> 1) - 1) & 1, abort_flag, p.status)) break;
+        if (i >= AS && !warp_wait(a_empty(sa), ((i / AS) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         PS_TC_TRACE(16 + (i & 255) * 8 + 2, t == 0);
         const unsigned char* row = gbase + (w_addr(sw) - base) + sub * 8192 + rin * 64;
