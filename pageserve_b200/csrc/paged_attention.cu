@@ -881,6 +881,361 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill / chunked-prefill attention on tcgen05 (D = 128, block 16).
+// One CTA = one kv head x 128 query rows (128/G tokens x the G heads of the
+// group, row r = token*G + g) x all of their causal key range, in 128-key
+// tiles. Roles (192 threads):
+//   warp 0    TMA producer: the Q tile once (3-D box 64 x G x 128/G per D
+//             half), then per key tile 8 blocks x 2 halves of K and of V
+//             (3-D boxes 64 x 1 x 16 from the paged cache, 128B swizzle)
+//             into a 2-stage ring; block-table entries prefetched per lane
+//   warp 1    TMEM allocator + MMA issuer: S_j = Q K_j^T into one of two
+//             TMEM S buffers (M=128, N=128, K=16 x 8, both operands K-major
+//             in shared memory), then O += P_{j-1} V_{j-1} (A = P from TMEM,
+//             B = V read MN-major from its [key][D] tile)
+//   warps 2-5 softmax, one query row per thread (TMEM lane quarter w%4):
+//             S from TMEM, causal mask, online max/sum in the log2 domain,
+//             O rescaled in TMEM when the max moves, P written to TMEM as
+//             bf16/f16 (the PV MMA's A operand); at the end O / l to global
+// TMEM: S0 | S1 | O (128 columns each) | P (64 columns). Every wait is
+// bounded (kErrTimeout, then the roles drain and TMEM is freed).
+constexpr int kPtKeys = 128;                      // keys per tile
+constexpr int kPtQBytes = 128 * 128 * 2;          // Q tile: 2 halves x 16 KB
+constexpr int kPtKVBytes = kPtKeys * 128 * 2;     // K (or V) tile: 2 halves x 16 KB
+constexpr int kPtStages = 2;
+constexpr int kPtThreads = 192;
+
+PS_DEVICE void tc_fence_before_a() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+PS_DEVICE void tc_fence_after_a() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+PS_DEVICE uint64_t desc_sw128_a(uint32_t addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // 8-row group stride
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;           // 128B swizzle
+  return d;
+}
+// kind::f16 instruction descriptor, f32 accumulate; b_mn: B is MN-major.
+__host__ __device__ constexpr uint32_t idesc_a(bool bf16, int m, int n, bool b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+PS_DEVICE void mma_ss_a(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+PS_DEVICE void mma_ts_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+PS_DEVICE void mma_commit_a(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+PS_DEVICE void tmem_ld32_a(uint32_t addr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+PS_DEVICE void tmem_st16_a(uint32_t addr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+PS_DEVICE void tmem_st32f_a(uint32_t addr, const float* f) {
+  uint32_t v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(f[i]);
+  tmem_st16_a(addr, v);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(f[16 + i]);
+  tmem_st16_a(addr + 16, v);
+}
+PS_DEVICE void tmem_wait_st_a() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 2^x by the MUFU approximation (relative error ~2^-22; 2^-inf = 0): the
+// probabilities are rounded to 16 bits right after.
+PS_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPtThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                   const __grid_constant__ CUtensorMap kmap,
+                                                                   const __grid_constant__ CUtensorMap vmap,
+                                                                   const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - raw);
+  const uint32_t q_sa = base;
+  auto k_sa = [&](int s) { return base + kPtQBytes + s * 2 * kPtKVBytes; };
+  auto v_sa = [&](int s) { return k_sa(s) + kPtKVBytes; };
+  const uint32_t bars = base + kPtQBytes + kPtStages * 2 * kPtKVBytes;
+  auto kv_full = [&](int s) { return bars + 8 * s; };
+  auto kv_empty = [&](int s) { return bars + 8 * (2 + s); };
+  auto s_full = [&](int b) { return bars + 8 * (4 + b); };
+  auto s_free = [&](int b) { return bars + 8 * (6 + b); };
+  const uint32_t q_full = bars + 8 * 8;
+  const uint32_t p_full = bars + 8 * 9;
+  const uint32_t pv_done = bars + 8 * 10;
+  unsigned char* misc = gbase + kPtQBytes + kPtStages * 2 * kPtKVBytes + 8 * 12;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int q0 = p.cu_q[b];
+  const int T_b = p.cu_q[b + 1] - q0;
+  const int sp = p.start_pos[b];
+  const int ctx = sp + T_b;
+  const int G = p.G;
+  const int TQ = 128 / G;  // tokens per tile
+  const int ntile_rows = (T_b + TQ - 1) / TQ;
+  const int rt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // longest key ranges first
+  if (T_b <= 0 || rt >= ntile_rows) return;
+  if (T_b > p.max_q_len || ctx > p.max_ctx || sp < 0 || ctx > p.max_blocks * p.block_size) {
+    if (threadIdx.x == 0) record_error(p.status, kErrShape);
+    return;
+  }
+  const int tq0 = rt * TQ;
+  const int kv_end = min(ctx, sp + min(T_b, tq0 + TQ));  // keys the tile's last row sees
+  const int ntiles = (kv_end + kPtKeys - 1) / kPtKeys;
+  const int32_t* table = p.tables + static_cast<long long>(b) * p.max_blocks;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kPtStages; ++s) {
+      mbar_init_a(kv_full(s), 1);
+      mbar_init_a(kv_empty(s), 1);
+    }
+    for (int bb = 0; bb < 2; ++bb) {
+      mbar_init_a(s_full(bb), 1);
+      mbar_init_a(s_free(bb), 4);
+    }
+    mbar_init_a(q_full, 1);
+    mbar_init_a(p_full, 4);
+    mbar_init_a(pv_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before_a();
+  __syncthreads();
+  tc_fence_after_a();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s0 = tmem, t_o = tmem + 256, t_p = tmem + 384;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer --
+    if (lane == 0) {
+      mbar_expect_tx_a(q_full, kPtQBytes);
+      for (int half = 0; half < 2; ++half)
+        tma_load_3d(q_sa + half * (kPtQBytes / 2), &qmap, q_full, half * 64, h * G, q0 + tq0);
+    }
+    __syncwarp();
+    const int last_blk = (kv_end - 1) / 16;  // later tile blocks reload it (finite data, masked keys)
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j % kPtStages;
+      if (j >= kPtStages && !warp_wait_a(kv_empty(s), ((j / kPtStages) - 1) & 1, abort_flag, p.status)) break;
+      int blk = j * 8 + (lane & 7);
+      if (blk > last_blk) blk = last_blk;
+      int phys = table[blk];
+      if (phys < 0 || phys >= p.num_blocks) {
+        record_error(p.status, kErrBlockId);
+        phys = 0;
+      }
+      int physj[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) physj[i] = __shfl_sync(0xffffffffu, phys, i);
+      if (lane == 0) {
+        mbar_expect_tx_a(kv_full(s), 2 * kPtKVBytes);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = physj[i] * 16;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            tma_load_3d(k_sa(s) + half * (kPtKVBytes / 2) + i * 2048, &kmap, kv_full(s), half * 64, h, row);
+            tma_load_3d(v_sa(s) + half * (kPtKVBytes / 2) + i * 2048, &vmap, kv_full(s), half * 64, h, row);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA --
+    constexpr uint32_t id_qk = idesc_a(kBf16, 128, 128, false);
+    constexpr uint32_t id_pv = idesc_a(kBf16, 128, 128, true);
+    bool ok = warp_wait_a(q_full, 0, abort_flag, p.status);
+    for (int j = 0; ok && j <= ntiles; ++j) {
+      if (j < ntiles) {
+        const int s = j % kPtStages, sb = j & 1;
+        ok = warp_wait_a(kv_full(s), (j / kPtStages) & 1, abort_flag, p.status);
+        if (ok && j >= 2) ok = warp_wait_a(s_free(sb), ((j >> 1) - 1) & 1, abort_flag, p.status);
+        if (!ok) break;
+        tc_fence_after_a();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // D = 128 in 8 steps of 16 (64 per 128B-swizzled half)
+            const uint32_t off = (kk >> 2) * (kPtQBytes / 2) + (kk & 3) * 32;
+            mma_ss_a(t_s0 + sb * 128, desc_sw128_a(q_sa + off, 0), desc_sw128_a(k_sa(s) + off, 0), id_qk,
+                     kk > 0 ? 1u : 0u);
+          }
+          mma_commit_a(s_full(sb));
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        // O += P_{j-1} V_{j-1}: V tile [key][D] read MN-major (D halves 16 KB apart)
+        const int s = (j - 1) % kPtStages;
+        ok = warp_wait_a(p_full, (j - 1) & 1, abort_flag, p.status);
+        if (!ok) break;
+        tc_fence_after_a();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 128 keys in 8 steps of 16
+            mma_ts_a(t_o, t_p + kk * 8, desc_sw128_a(v_sa(s) + kk * 16 * 128, kPtKVBytes / 2), id_pv,
+                     (j > 1 || kk > 0) ? 1u : 0u);
+          mma_commit_a(kv_empty(s));
+          mma_commit_a(pv_done);
+        }
+        __syncwarp();
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- softmax --
+    // One pass over S per tile (128 scores in registers). The running max
+    // used for P and O ("m_ref") only moves when a row's max grows by more
+    // than 8 (log2 domain), so O is rescaled in TMEM rarely; P <= 2^8 stays
+    // well inside the 16-bit range and l uses the same reference.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // this thread's query row (TMEM lane)
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int tok = tq0 + r / G;
+    const int g = r % G;
+    const int qpos = sp + tok;           // causal limit: keys <= qpos
+    const bool row_ok = tok < T_b;
+    float m_ref = -FLT_MAX, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      ok = warp_wait_a(s_full(sb), (j >> 1) & 1, abort_flag, p.status);
+      if (!ok) break;
+      tc_fence_after_a();
+      const int key0 = j * kPtKeys;
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_a(t_s0 + sb * 128 + c * 32 + lane_off, sv + 32 * c);
+      // keys past a row's causal limit or the context get -inf (whole-warp fast path when none does)
+      const bool full = __all_sync(0xffffffffu, key0 + kPtKeys - 1 <= qpos && key0 + kPtKeys <= kv_end);
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        float x = sv[i] * p.scale_log2;
+        if (!full && (key0 + i > qpos || key0 + i >= kv_end)) x = -INFINITY;  // 2^(-inf - m) = 0 for any m
+        sv[i] = x;
+        mx = fmaxf(mx, x);
+      }
+      float alpha = 1.f;
+      bool moved = false;
+      if (mx > m_ref + 8.f) {
+        const float m_new = mx;
+        alpha = (m_ref == -FLT_MAX) ? 0.f : ex2_approx(m_ref - m_new);
+        m_ref = m_new;
+        moved = true;
+      }
+      // O must hold P_{j-1} V_{j-1} before it is rescaled and P overwritten
+      if (j >= 1) {
+        ok = warp_wait_a(pv_done, (j - 1) & 1, abort_flag, p.status);
+        if (!ok) break;
+        tc_fence_after_a();
+        if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32_a(t_o + c * 32 + lane_off, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tmem_st32f_a(t_o + c * 32 + lane_off, v);
+          }
+        }
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(sv[32 * c + i] - m_ref);      // -inf -> 0
+          const float p1 = ex2_approx(sv[32 * c + i + 1] - m_ref);
+          sum += p0 + p1;
+          pk[i / 2] = pack2<T>(p0, p1);
+        }
+        tmem_st16_a(t_p + c * 16 + lane_off, pk);
+      }
+      tmem_wait_st_a();
+      tc_fence_before_a();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_a(s_free(sb));
+        mbar_arrive_a(p_full);
+      }
+      l = l * alpha + sum;
+    }
+    // epilogue: O / l
+    if (ok) ok = warp_wait_a(pv_done, (ntiles - 1) & 1, abort_flag, p.status);
+    if (ok) {
+      tc_fence_after_a();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* dst = static_cast<T*>(p.out) + (static_cast<long long>(q0 + tok) * p.Hq + h * G + g) * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32_a(t_o + c * 32 + lane_off, v);
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = v[i + e] * inv;
+            *reinterpret_cast<uint4*>(dst + c * 32 + i) = pack8<T>(o);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before_a();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_a();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
 // Merge split partials: one warp per (sequence, chunk token, q head) row.
 template <typename T, int D>
 __global__ void combine_kernel(const AttnParams p) {
@@ -1047,14 +1402,64 @@ int launch_decode_tma(AttnParams& p, int num_seqs, int max_q_len, cudaStream_t s
   return ps_host::check_launch("paged_attention(combine)");
 }
 
+// The q tensor [total_q][Hq][128] as a 3-D TMA tensor, box 64 x G x 128/G
+// (one 128-row query tile per D half), 128B swizzle.
+bool make_q_map(CUtensorMap* map, const void* q, bool bf16, int total_q, int Hq, int G) {
+  auto fn = attn_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(Hq), static_cast<cuuint64_t>(total_q)};
+  cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(Hq) * 128 * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(128 / G)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(q),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool prefill_tc_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("PS_ATTN_PREFILL_TC");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
+template <typename T>
+int launch_prefill_tc(AttnParams& p, int num_seqs, int max_q_len, int total_q, cudaStream_t s) {
+  CUtensorMap qm, km, vm;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (!make_q_map(&qm, p.q, bf16, total_q, p.Hq, p.G) || !make_kv_map(&km, p.k_cache, bf16, p.num_blocks, p.Hkv) ||
+      !make_kv_map(&vm, p.v_cache, bf16, p.num_blocks, p.Hkv)) {
+    ps_host::set_error("paged_attention: cuTensorMapEncodeTiled failed (prefill)");
+    return PS_ERR_CUDA;
+  }
+  const int smem = kPtQBytes + kPtStages * 2 * kPtKVBytes + 1024 + 1024;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(prefill_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      ps_host::set_error("paged_attention: cannot reserve %d bytes of shared memory", smem);
+      return PS_ERR_CUDA;
+    }
+    attr = true;
+  }
+  const int tq = 128 / p.G;
+  dim3 grid((max_q_len + tq - 1) / tq, p.Hkv, num_seqs);
+  ps_host::launch(prefill_tc_kernel<T>, grid, kPtThreads, smem, s, qm, km, vm, p);
+  ps_host::count_launch();
+  return ps_host::check_launch("paged_attention(prefill, tcgen05)");
+}
+
 template <typename T, int D>
-int launch(AttnParams& p, int num_seqs, int max_q_len, int max_ctx, cudaStream_t s) {
+int launch(AttnParams& p, int num_seqs, int max_q_len, int max_ctx, cudaStream_t s, int total_q) {
   const bool decode = max_q_len * p.G <= 16;
   if constexpr (D == 128) {
     // the serving layout: TMA needs 16-key blocks and 16-byte aligned rows
-    if (decode && p.block_size == 16 && static_cast<long long>(p.num_blocks) * 16 < (1LL << 31) &&
-        ps_host::aligned(p.k_cache, 16) && ps_host::aligned(p.v_cache, 16))
-      return launch_decode_tma<T>(p, num_seqs, max_q_len, s);
+    const bool tma_ok = p.block_size == 16 && static_cast<long long>(p.num_blocks) * 16 < (1LL << 31) &&
+                        ps_host::aligned(p.k_cache, 16) && ps_host::aligned(p.v_cache, 16);
+    if (decode && tma_ok) return launch_decode_tma<T>(p, num_seqs, max_q_len, s);
+    if (!decode && tma_ok && prefill_tc_enabled() && 128 % p.G == 0 && ps_host::aligned(p.q, 16) &&
+        ps_host::aligned(p.out, 16))
+      return launch_prefill_tc<T>(p, num_seqs, max_q_len, total_q, s);
   }
   const int stage_smem = kStages * 2 * Tile<D>::kBytes;
   const int merge_smem = kWarps * 16 * D * 4 + 2 * kWarps * 16 * 4;
@@ -1160,11 +1565,11 @@ int ps_paged_attention(void* out, const void* q, const void* k_cache, const void
   p.num_seqs = num_seqs;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_BF16) {
-    if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s);
-    if (D == 64) return launch<__nv_bfloat16, 64>(p, num_seqs, max_q_len, max_ctx, s);
+    if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s, total_q);
+    if (D == 64) return launch<__nv_bfloat16, 64>(p, num_seqs, max_q_len, max_ctx, s, total_q);
   } else if (dtype == PS_F16) {
-    if (D == 128) return launch<__half, 128>(p, num_seqs, max_q_len, max_ctx, s);
-    if (D == 64) return launch<__half, 64>(p, num_seqs, max_q_len, max_ctx, s);
+    if (D == 128) return launch<__half, 128>(p, num_seqs, max_q_len, max_ctx, s, total_q);
+    if (D == 64) return launch<__half, 64>(p, num_seqs, max_q_len, max_ctx, s, total_q);
   } else {
     ps_host::set_error("paged_attention: dtype must be bf16 or f16");
     return PS_ERR_UNSUPPORTED;
@@ -1295,11 +1700,11 @@ extern "C" int ps_paged_attention_noalloc(void* out, const void* q, const void* 
   p.num_seqs = num_seqs;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_BF16) {
-    if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s);
-    if (D == 64) return launch<__nv_bfloat16, 64>(p, num_seqs, max_q_len, max_ctx, s);
+    if (D == 128) return launch<__nv_bfloat16, 128>(p, num_seqs, max_q_len, max_ctx, s, total_q);
+    if (D == 64) return launch<__nv_bfloat16, 64>(p, num_seqs, max_q_len, max_ctx, s, total_q);
   } else if (dtype == PS_F16) {
-    if (D == 128) return launch<__half, 128>(p, num_seqs, max_q_len, max_ctx, s);
-    if (D == 64) return launch<__half, 64>(p, num_seqs, max_q_len, max_ctx, s);
+    if (D == 128) return launch<__half, 128>(p, num_seqs, max_q_len, max_ctx, s, total_q);
+    if (D == 64) return launch<__half, 64>(p, num_seqs, max_q_len, max_ctx, s, total_q);
   } else {
     ps_host::set_error("paged_attention_noalloc: dtype must be bf16 or f16");
     return PS_ERR_UNSUPPORTED;
