@@ -23,6 +23,10 @@ model serving the same 64 sequences, so the work is fixed (strong scaling).
 --impl reference: the reference algorithm's CPU path (the oracle port of
 engine/model.py, one forward_step per sequence as engine/runner.py:65-79
 does), on a bounded sample of the same workload, all host threads.
+--config 5: BASELINE config 5 instead (Qwen2.5-32B shape, 64 layers, hidden
+5120, 40/8 heads, intermediate 27648, untied vocab 152064, int8): a decode
+step of 128 sequences at context 4096, tensor parallel over --gpus N ranks
+(one GPU holds the whole model and its 137 GB KV cache at N = 1).
 """
 
 from __future__ import annotations
@@ -43,6 +47,15 @@ METRIC = "decode tok/s (Qwen2.5-3B-shape W8A16, bs64)"
 UNIT = "tok/s"
 N_DECODE, CTX, PREFILL = 64, 2048, 512
 BLOCK = 16
+CONFIG = 4
+SHAPE_NAME = "qwen2.5-3b"
+
+
+def _use_config5():
+    """32B-shape int8 decode, B = 128 at context 4096."""
+    global METRIC, N_DECODE, CTX, PREFILL, CONFIG, SHAPE_NAME
+    METRIC = "decode tok/s (Qwen2.5-32B-shape W8A16 TP, bs128 @ctx 4096)"
+    N_DECODE, CTX, PREFILL, CONFIG, SHAPE_NAME = 128, 4096, 0, 5, "qwen2.5-32b"
 
 
 def _peaks():
@@ -54,14 +67,26 @@ def _peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+def _shape():
+    from pageserve_b200 import synthetic
+    return synthetic.SHAPES[SHAPE_NAME]
+
+
 def _config(extra=None):
-    c = {"workload": ("BASELINE config 4: Qwen2.5-3B-shape int8 mixed step, 64 decode seqs @ctx 2048 "
-                      f"+ one {PREFILL}-token prefill chunk, block 16") if PREFILL else
-                     "Qwen2.5-3B-shape int8 decode-only step (config 4 without its prefill chunk): 64 decode seqs "
-                     "@ctx 2048, block 16",
-         "model": "qwen2.5-3b-shape (random init)", "layers": 36, "global_batch": N_DECODE,
+    if CONFIG == 5:
+        wl = ("BASELINE config 5: Qwen2.5-32B-shape int8 decode step, 128 seqs @ctx 4096, block 16, "
+              "tensor parallel over the job's GPUs")
+    elif PREFILL:
+        wl = ("BASELINE config 4: Qwen2.5-3B-shape int8 mixed step, 64 decode seqs @ctx 2048 "
+              f"+ one {PREFILL}-token prefill chunk, block 16")
+    else:
+        wl = ("Qwen2.5-3B-shape int8 decode-only step (config 4 without its prefill chunk): 64 decode seqs "
+              "@ctx 2048, block 16")
+    c = {"workload": wl,
+         "model": f"{SHAPE_NAME}-shape (random init)", "layers": _shape().num_layers, "global_batch": N_DECODE,
          "prefill_tokens_per_step": PREFILL, "seq_len": CTX, "kv_dtype": "bf16", "weights": "int8 per-channel",
-         "l2": "inputs larger than L2 (~8 GB streamed per step)"}
+         "l2": ("inputs larger than L2 (~8 GB of weights + KV streamed per step)" if CONFIG == 4 else
+                "inputs larger than L2 (~170 GB of weights + KV per step over all ranks)")}
     if extra:
         c.update(extra)
     return c
@@ -131,10 +156,10 @@ def build_workload(device, seed=0, tp=None, tp_comm="auto"):
     from pageserve_b200 import synthetic
     from pageserve_b200.model import PagedCausalLM
 
-    shape = synthetic.QWEN25_3B
+    shape = synthetic.SHAPES[SHAPE_NAME]
     sd = synthetic.TorchStateDict(shape, seed=seed, device=device)
     m = PagedCausalLM.from_state_dict(sd, shape, device=device, dtype=torch.bfloat16, quantize=True,
-                                      max_position=4096, tp=tp, tp_comm=tp_comm, tp_max_tokens=N_DECODE + PREFILL)
+                                      max_position=max(4096, CTX), tp=tp, tp_comm=tp_comm, tp_max_tokens=N_DECODE + PREFILL)
     del sd
     torch.cuda.empty_cache()
     nblk_dec = CTX // BLOCK
@@ -184,14 +209,15 @@ def time_events(fn, iters):
 
 # ncu summaries (profiles/) of the step's kernel classes: same kernel, same shape
 PROFILE_OF = {"gate_up": "linear_tc_gate_up_swiglu_M576.md", "down": "linear_tc_down_M576.md",
-              "qkv": "linear_tc_qkv_M576.md", "attn_decode": "decode_tma_cfg4.md"}
+              "qkv": "linear_tc_qkv_M576.md", "attn_decode": "decode_tma_cfg4.md",
+              "attn_prefill": "prefill_tc_T512.md"}
 
 
 def profile_traffic(kernel):
     """dram__bytes_read.sum + dram__bytes_write.sum per launch of `kernel`
     from its committed ncu summary (None when there is none)."""
     name = PROFILE_OF.get(kernel)
-    if not name or PREFILL != 512:  # the captures are of the config-4 shapes (576 tokens)
+    if not name or PREFILL != 512 or CONFIG != 4:  # the captures are of the config-4 shapes (576 tokens)
         return None, None
     path = ROOT / "profiles" / name
     try:
@@ -206,7 +232,7 @@ def profile_traffic(kernel):
 
 def kernel_breakdown(m, w, peaks):
     """Each main kernel of the step timed alone (CUDA-graph replay between
-    CUDA events), rotating over the 36 layers' weights / caches so nothing
+    CUDA events), rotating over the layers' weights / caches so nothing
     is served from L2."""
     import torch
 
@@ -257,7 +283,7 @@ def kernel_breakdown(m, w, peaks):
     byts = V * H * 2 + 2 * xl.shape[0] * (H + V)
     res["lm_head"] = {"ms": ms, "M": xl.shape[0], "N": V, "K": H, "gbs": byts / ms / 1e6, "bytes": byts,
                       "tflops": 2.0 * xl.shape[0] * V * H / ms / 1e9, "flops": 2.0 * xl.shape[0] * V * H}
-    # decode attention: 64 sequences at ctx 2048, rotating over layer caches
+    # decode attention: the decode sequences at their context, rotating over layer caches
     meta = m.make_meta([1] * N_DECODE, [CTX - 1] * N_DECODE, w["tables"][:N_DECODE])
     q = torch.randn(N_DECODE, m.heads_local, m.head_dim, device=dev, dtype=torch.bfloat16)
     aws = AttentionWorkspace()
@@ -297,9 +323,10 @@ def kernel_breakdown(m, w, peaks):
 def cpu_baseline_sample(layers_sampled=6, decode_seqs_sampled=8):
     """The reference algorithm on the host cores (oracle port of
     engine/model.py, per-sequence forward_step like engine/runner.py:65-79):
-    a 1-layer 3B-shape model runs `decode_seqs_sampled` decode sequences at
-    context 2048 and the 512-token prefill chunk; per-layer and head time are
-    scaled to 36 layers and 64 decode sequences."""
+    a `layers_sampled`-layer model of the workload's shape runs
+    `decode_seqs_sampled` decode sequences at the workload's context (and the
+    prefill chunk, if any); per-layer and head time are scaled to the full
+    layer count and batch."""
     import numpy as np
     import torch
 
@@ -307,7 +334,8 @@ def cpu_baseline_sample(layers_sampled=6, decode_seqs_sampled=8):
     from pageserve_b200 import synthetic
 
     torch.set_num_threads(os.cpu_count() or 1)
-    shape = synthetic.QWEN25_3B.with_layers(layers_sampled)
+    full = synthetic.SHAPES[SHAPE_NAME]
+    shape = full.with_layers(layers_sampled)
     sd = synthetic.generate_state_dict(shape, seed=0)
     o = OracleCausalLM(sd, shape, quantize=True, max_position=4096)
     del sd
@@ -324,11 +352,12 @@ def cpu_baseline_sample(layers_sampled=6, decode_seqs_sampled=8):
     if PREFILL:
         o.forward_step(rng.integers(0, shape.vocab, size=PREFILL), tabs[-1], 0, timings=t_pre)
     wall = time.perf_counter() - t0
-    per_dec = (t_dec["layers"] / layers_sampled * 36 + t_dec["head"]) / decode_seqs_sampled
-    step = N_DECODE * per_dec + ((t_pre["layers"] / layers_sampled * 36 + t_pre["head"]) if PREFILL else 0.0)
+    L = full.num_layers
+    per_dec = (t_dec["layers"] / layers_sampled * L + t_dec["head"]) / decode_seqs_sampled
+    step = N_DECODE * per_dec + ((t_pre["layers"] / layers_sampled * L + t_pre["head"]) if PREFILL else 0.0)
     return {"value": N_DECODE / step, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
             "sample": (f"oracle port of the reference step (numpy/BLAS, per-sequence forward_step); "
-                       f"{layers_sampled} of 36 layers, {decode_seqs_sampled} of 64 decode seqs"
+                       f"{layers_sampled} of {L} layers, {decode_seqs_sampled} of {N_DECODE} decode seqs"
                        + (f" + the {PREFILL}-token chunk" if PREFILL else "")
                        + f", scaled to the full step; sample wall {wall:.1f} s"),
             "step_s": step}
@@ -345,9 +374,9 @@ def run_reference(args):
     # each step is a bounded sample (about 1 s per sampled layer) sized so the
     # whole run stays within a few minutes
     n = max(1, args.warmup) + max(1, args.steps)
-    layers = max(1, min(6, int(150 / n)))
+    layers = max(1, min(6, int(150 / n))) if CONFIG == 4 else 1
     for i in range(n):
-        cb = cpu_baseline_sample(layers_sampled=layers, decode_seqs_sampled=4)
+        cb = cpu_baseline_sample(layers_sampled=layers, decode_seqs_sampled=4 if CONFIG == 4 else 1)
         if i >= max(1, args.warmup):
             vals.append(cb["value"])
     v = statistics.median(vals)
@@ -435,7 +464,7 @@ def run_gpu(args):
         _finish(g, m, world)
         return
     # dominant kernel: the largest per-step time share among the measured classes
-    per_step = {k: v["ms"] * (36 if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode", "attn_prefill") else 1)
+    per_step = {k: v["ms"] * (len(m.fused) if k in ("qkv", "o_proj", "gate_up", "down", "attn_decode", "attn_prefill") else 1)
                 for k, v in kb.items()}
     dom = max(per_step, key=per_step.get)
     d = kb[dom]
@@ -452,7 +481,9 @@ def run_gpu(args):
         roof = {"kernel": dom, "bound": "hbm", "achieved": d["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": d["gbs"] / peaks["hbm_gbs"], "traffic": traffic, "algorithmic_per_launch": d["bytes"],
                 "peak_source": peaks["source"], "traffic_source": traffic_src}
-    cpu = cpu_baseline_sample() if (not args.no_cpu_baseline and world == 1) else None
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        cpu = cpu_baseline_sample() if CONFIG == 4 else cpu_baseline_sample(layers_sampled=1, decode_seqs_sampled=1)
     clocks = clk.summary()
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -469,7 +500,7 @@ def run_gpu(args):
             "kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
                         for k, v in kb.items()},
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "clocks": clocks}
+            "clocks": clocks, "hbm_peak_gb_rank0": round(torch.cuda.max_memory_allocated(device) / 1e9, 2)}
     print(json.dumps(line), flush=True)
     _finish(g, m, world)
 
@@ -498,8 +529,12 @@ def main():
                     help="prefill chunk tokens per step (default 512 = BASELINE config 4; 0 = decode-only step)")
     ap.add_argument("--tp-comm", default="auto", choices=["auto", "fused", "nccl"],
                     help="N>1 tensor parallelism: row-parallel reduction transport")
+    ap.add_argument("--config", type=int, default=4, choices=[4, 5],
+                    help="BASELINE configuration: 4 = 3B-shape mixed step (default), 5 = 32B-shape TP decode")
     args = ap.parse_args()
     global PREFILL
+    if args.config == 5:
+        _use_config5()
     if args.prefill is not None:
         PREFILL = max(0, args.prefill)
     if args.warmup < 3:
