@@ -616,6 +616,13 @@ Plan plan(int M, int N, int K, bool int8) {
         splits = 148 / (nt1 * m_tiles);
         if (splits > 4) splits = 4;
         if (splits < 1) splits = 1;
+      } else if (pl.bm == 128) {
+        // one token tile of 65..128 tokens: split K to about one wave
+        // (M=128 q|k|v N=3584 K=5120: 25.6 -> 17.4 us; o_proj N=5120
+        // K=2560: 16.2 -> 14.2 us)
+        splits = 148 / (nt1 * m_tiles);
+        if (splits > 8) splits = 8;
+        if (splits < 2) splits = 2;
       }
     }
   } else {

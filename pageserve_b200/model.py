@@ -16,6 +16,7 @@ then the final rmsnorm, the bf16 lm_head and an on-device argmax.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from types import SimpleNamespace
 
@@ -328,6 +329,13 @@ class PagedCausalLM:
         self.rope_cos, self.rope_sin = build_rope_table_f32(self.max_position_embeddings, self.head_dim, theta,
                                                             self.device)
         self.attn_ws = AttentionWorkspace()
+        # Prefill and decode attention of one step are independent (disjoint
+        # output rows, read-only q and caches): the prefill runs go to a side
+        # stream (own workspace) so their small grid overlaps the HBM-bound
+        # decode kernel; PS_ATTN_CONCURRENT=0 runs them back to back.
+        self.attn_ws_side = AttentionWorkspace()
+        self._attn_side = torch.cuda.Stream(device=self.device)
+        self._attn_concurrent = os.environ.get("PS_ATTN_CONCURRENT", "1") != "0"
         self.lin_ws = LinearWorkspace()
         if tp_comm not in ("fused", "nccl", "auto"):
             raise ValueError(f"tp_comm must be 'fused', 'nccl' or 'auto', not {tp_comm!r}")
@@ -404,9 +412,7 @@ class PagedCausalLM:
                                                 positions.data_ptr(), slots.data_ptr(), self.rope_cos.data_ptr(),
                                                 self.rope_sin.data_ptr(), self.max_position_embeddings, T, hq, hkv,
                                                 d, num_slots, _lib.dtype_code(self.dtype), stream), "rope_qkv")
-            for (s, e, _) in runs:
-                paged_attention(q, kc, vc, meta.block_tables[s:e], meta.cu_q[s:e + 1], meta.start_pos[s:e],
-                                max(meta.q_lens[s:e]), max(meta.ctx_lens[s:e]), out=attn, workspace=self.attn_ws)
+            self._attention(q, kc, vc, meta, runs, attn)
             if comm is not None:
                 comm.linear_push(attn.view(T, hq * d), fl.o, 0, workspace=self.lin_ws)
                 h = comm.allreduce_rmsnorm(x, fl.post_ln, self.rms_eps, 0)
@@ -432,6 +438,34 @@ class PagedCausalLM:
                 x = x.index_select(0, logits_rows)
             x = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
         return linear16(x, self.lm_head_w, workspace=self.lin_ws)
+
+    def _attention(self, q, kc, vc, meta, runs, attn) -> None:
+        """Paged attention of every run into its rows of ``attn``; with both
+        kinds present, the prefill runs on the side stream (forked after the
+        KV write, joined before o_proj), launched first so its CTAs start
+        before the decode grid fills the SMs."""
+        def run(s, e, ws):
+            paged_attention(q, kc, vc, meta.block_tables[s:e], meta.cu_q[s:e + 1], meta.start_pos[s:e],
+                            max(meta.q_lens[s:e]), max(meta.ctx_lens[s:e]), out=attn, workspace=ws)
+        kinds = {d for (_, _, d) in runs}
+        if not (self._attn_concurrent and len(kinds) == 2):
+            for (s, e, _) in runs:
+                run(s, e, self.attn_ws)
+            return
+        main = torch.cuda.current_stream(self.device)
+        side = self._attn_side
+        fork, join = torch.cuda.Event(), torch.cuda.Event()
+        fork.record(main)
+        side.wait_event(fork)
+        with torch.cuda.stream(side):
+            for (s, e, dec) in runs:
+                if not dec:
+                    run(s, e, self.attn_ws_side)
+        join.record(side)
+        for (s, e, dec) in runs:
+            if dec:
+                run(s, e, self.attn_ws)
+        main.wait_event(join)
 
     def close(self) -> None:
         """Release the fused all-reduce buffers and peer mappings (call on
