@@ -13,6 +13,8 @@ short for its context raises IndexError (engine/paged_attention.py:77, 95).
 
 from __future__ import annotations
 
+import itertools
+
 import numpy as np
 
 
@@ -44,15 +46,27 @@ def pack_metadata(q_lens, start_pos, block_tables, block_size: int, num_blocks: 
     skip them and set the device status word)."""
     ctx = validate_tables(q_lens, start_pos, block_tables, block_size)
     B = len(q_lens)
-    mb = max_blocks or max(1, max(len(t) for t in block_tables))
-    tab = np.full((B, mb), -1, dtype=np.int32)
-    for b, t in enumerate(block_tables):
-        n = min(len(t), mb)
-        if n < (ctx[b] + block_size - 1) // block_size:
-            raise IndexError(f"sequence {b}: context {ctx[b]} exceeds max_blocks {mb}")
-        tab[b, :n] = np.asarray(t[:n], dtype=np.int64)
-        if num_blocks is not None and n and (tab[b, :n].min() < 0 or tab[b, :n].max() >= num_blocks):
+    lens = [len(t) for t in block_tables]
+    mb = max_blocks or max(1, max(lens))
+    # one flat conversion of all tables and vectorised checks: this runs on
+    # the host between steps, so its cost is part of the end-to-end step
+    n = np.minimum(np.asarray(lens, np.int64), mb)
+    short = np.nonzero(n < (np.asarray(ctx, np.int64) + block_size - 1) // block_size)[0]
+    if short.size:
+        b = int(short[0])
+        raise IndexError(f"sequence {b}: context {ctx[b]} exceeds max_blocks {mb}")
+    total = int(n.sum())
+    flat = np.fromiter(itertools.chain.from_iterable(t[:mb] if len(t) > mb else t for t in block_tables),
+                       dtype=np.int64, count=total)
+    if num_blocks is not None and total:
+        bad = (flat < 0) | (flat >= num_blocks)
+        if bad.any():
+            b = int(np.searchsorted(np.cumsum(n), int(np.argmax(bad)), side="right"))
             raise IndexError(f"sequence {b}: block id outside the pool of {num_blocks} blocks")
+    tab = np.full((B, mb), -1, dtype=np.int32)
+    if total:
+        starts = np.cumsum(n) - n
+        tab[np.repeat(np.arange(B), n), np.arange(total) - np.repeat(starts, n)] = flat
     cu = np.zeros(B + 1, dtype=np.int32)
     cu[1:] = np.cumsum(np.asarray(q_lens, dtype=np.int64))
     buf = np.concatenate([cu, np.asarray(start_pos, np.int32), tab.reshape(-1)])
