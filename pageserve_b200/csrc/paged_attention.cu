@@ -1389,7 +1389,9 @@ int launch_decode_tma(AttnParams& p, int num_seqs, int max_q_len, cudaStream_t s
   // whatever the mix of context lengths.
   p.balanced = p.num_splits > 1 ? 1 : 0;
   const long long pairs = static_cast<long long>(num_seqs) * p.Hkv;
-  dim3 grid = p.balanced ? dim3(static_cast<unsigned>(pairs > 2 * 148 ? pairs : 2 * 148))
+  long long slots = 2 * 148;
+  if (const char* env = std::getenv("PS_ATTN_DECODE_GRID")) slots = std::atoll(env) > 0 ? std::atoll(env) : slots;  // tuning
+  dim3 grid = p.balanced ? dim3(static_cast<unsigned>(pairs > slots ? pairs : slots))
                          : dim3(p.num_splits, p.Hkv, num_seqs);
   ps_host::launch(decode_tma_kernel<T>, grid, 160, smem, s, km, vm, p);
   ps_host::count_launch();
