@@ -11,8 +11,9 @@
 // flop); decode-sized batches use NSUB = 1 for more CTAs.
 //
 // Roles (352 threads), each ring with its own full/empty mbarrier pair:
-//   warp 0      weight producer: TMA of the int8 tile (NSUB*128 x 64 B) into
-//               a deep ring (or the bf16 tile straight into the operand ring)
+//   warp 0      weight producer: one contiguous 8 KB bulk copy per 128-row
+//               block of the pre-tiled int8 weight (a 2-D TMA for row-major
+//               int8, or the 16-bit tile straight into the operand ring)
 //   warp 1      TMEM allocator; one elected lane issues
 //               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BM, K=16),
 //               NSUB x 4 per k-tile, and commits to the rings' empty barriers
@@ -23,11 +24,12 @@
 //               weight row per lane, K packed two bf16 per column), running up
 //               to that many k-tiles ahead of the MMA, which reads A from TMEM
 //               (tcgen05.mma ... [a_tmem]) and only the activations from
-//               shared memory; then they copy the accumulators from TMEM
-//               (tcgen05.ld 32x32b; warp w reads lane quarter w%4) into a
-//               token-major fp32 stage in shared memory
-//   all warps   epilogue from the stage: 8 consecutive outputs per thread
-//               (scale, bias, residual), 16-byte stores along output rows
+//               shared memory; then they run the epilogue
+// Epilogue without a K split: the accumulators are read from TMEM
+// (tcgen05.ld 32x32b; warp w reads lane quarter w%4), scaled, biased,
+// residual-added (the residual tile TMA-loaded into the output tile first)
+// or SiLU*up-combined, rounded into a token-major 16-bit tile and TMA-stored
+// (to y, or to every rank's receive slot when pushing).
 // The weight stream runs ahead independently of the MMA, so HBM latency is
 // hidden by the weight ring depth rather than by the MMA's commit chain.
 // Keeping the widened weights in TMEM takes their write and the MMA's read
@@ -35,10 +37,11 @@
 // this loop. bf16/f16 weights (the lm_head) skip the widening: TMA lands
 // them in shared memory as the MMA's A operand directly.
 // Small-N shapes split K across CTAs: the splits of one output tile form a
-// thread-block cluster along z, and after the main loop each CTA reduces one
-// slice of the tile's token rows over all the splits' stages through
-// distributed shared memory (ld.shared::cluster, fixed split order), so the
-// partial sums never leave the chip and no second kernel runs.
+// thread-block cluster along z; after the main loop each CTA stages its fp32
+// partial tile, bulk-copies token-row slice j to cluster CTA j
+// (cp.async.bulk shared::cta -> shared::cluster), and each CTA sums its
+// slice over the splits in fixed order, so the partial sums never leave the
+// chip and no second kernel runs.
 //
 // Every mbarrier wait is bounded (about a second of clock64 cycles): on
 // timeout the kernel records kErrTimeout in the status word, stops issuing
