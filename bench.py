@@ -237,7 +237,7 @@ def kernel_breakdown(m, w, peaks):
     import torch
 
     from pageserve_b200.paged_attention import AttentionWorkspace, paged_attention
-    from pageserve_b200.quantization import LinearWorkspace, linear16, linear_swiglu, w8a16_linear
+    from pageserve_b200.quantization import LinearWorkspace, linear16, linear_swiglu
 
     dev = m.device
     T = N_DECODE + PREFILL
@@ -258,12 +258,12 @@ def kernel_breakdown(m, w, peaks):
             ctr[0] += 1
             if swiglu:  # the gate|up linear with SiLU*up in its epilogue, as the step runs it
                 outs["y"] = linear_swiglu(x, wgt)
-            else:
-                outs["y"] = w8a16_linear(x, wgt.q, wgt.scale, workspace=ws, q_tiled=wgt.tiled())
+            else:  # the step's path: the tiled int8 copy (the model keeps no row-major one)
+                outs["y"] = wgt.linear(x, workspace=ws)
         f()
         ms = time_events(f, 2 * L)
         wgt = get_w(m.fused[0])
-        N, K = wgt.q.shape
+        N, K = wgt.shape
         M = x.shape[0]
         flops = 2.0 * M * N * K
         byts = N * K + 4 * N + 2 * M * K + 2 * M * (N // 2 if swiglu else N)

@@ -130,9 +130,8 @@ class FusedAllReduce:
             raise ValueError(f"{M} tokens exceed the fused all-reduce capacity {self.max_tokens}")
         lib = _lib.load()
         if isinstance(weight, QuantizedWeight):
-            N = weight.q.shape[0]
-            w_ptr, wdt, wt_ptr, sc_ptr = weight.q.data_ptr(), _lib.PS_I8, weight.tiled().data_ptr(), \
-                weight.scale.data_ptr()
+            N = weight.shape[0]  # int8: the kernels read only the tiled copy
+            w_ptr, wdt, wt_ptr, sc_ptr = None, _lib.PS_I8, weight.tiled().data_ptr(), weight.scale.data_ptr()
         else:
             N = weight.shape[0]
             w_ptr, wdt, wt_ptr, sc_ptr = weight.data_ptr(), _lib.dtype_code(weight.dtype), None, None

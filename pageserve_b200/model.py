@@ -26,7 +26,7 @@ import torch
 from . import _lib
 from .batch import attention_runs, pack_metadata
 from .paged_attention import AttentionWorkspace, paged_attention
-from .quantization import LinearWorkspace, QuantizedWeight, linear16, linear_swiglu, w8a16_linear
+from .quantization import LinearWorkspace, QuantizedWeight, RowView, linear16, linear_swiglu
 
 Weight = torch.Tensor | QuantizedWeight
 
@@ -142,6 +142,26 @@ def _interleave_rows(a: Weight, b: Weight, dtype) -> Weight:
     if isinstance(a, QuantizedWeight):
         return QuantizedWeight.from_quantized(il(a.q, b.q), il(a.scale, b.scale), dtype)
     return il(a, b)
+
+
+def _one_copy(lw: "LayerWeights", fl: "FusedLayer", dtype) -> None:
+    """Keep one int8 copy of each of a layer's weights in HBM: the kernels'
+    tiled copies (built here, before any graph capture). The reference-facing
+    per-projection weights become row views of the fused q|k|v and gate|up
+    weights and the row-major copies are dropped (``q`` is rebuilt from the
+    tiled copy on access, outside the hot path). Done layer by layer so
+    loading never holds more than one layer's extra copies."""
+    for w in (fl.qkv, fl.o, fl.gate_up, fl.down):
+        if isinstance(w, QuantizedWeight):
+            w.release_row_major()
+    if isinstance(fl.qkv, QuantizedWeight):
+        nq, nk = lw.q_w.shape[0], lw.k_w.shape[0]
+        lw.q_w = RowView(fl.qkv, slice(0, nq), dtype)
+        lw.k_w = RowView(fl.qkv, slice(nq, nq + nk), dtype)
+        lw.v_w = RowView(fl.qkv, slice(nq + nk, nq + 2 * nk), dtype)
+    if isinstance(fl.gate_up, QuantizedWeight):
+        lw.gate_w = RowView(fl.gate_up, slice(0, None, 2), dtype)
+        lw.up_w = RowView(fl.gate_up, slice(1, None, 2), dtype)
 
 
 class StepMeta:
@@ -318,10 +338,8 @@ class PagedCausalLM:
                 input_ln=lw.input_ln, post_ln=lw.post_ln,
                 qkv=_cat_weights([lw.q_w, lw.k_w, lw.v_w], dtype), qkv_b=qkv_b, o=lw.o_w,
                 gate_up=_interleave_rows(lw.gate_w, lw.up_w, dtype), down=lw.down_w))
-        for fl in self.fused:  # kernel-side tiled int8 copies, built before any graph capture
-            for w in (fl.qkv, fl.o, fl.gate_up, fl.down):
-                if isinstance(w, QuantizedWeight):
-                    w.tiled()
+            _one_copy(lw, self.fused[-1], dtype)
+
         self.intermediate_size = (self.layers[0].gate_w.shape[0] if self.layers else 0)  # local under TP
         self.vocab_size = self.embed_tokens.shape[0]
         self.cos_cache, self.sin_cache = build_rope_cache(self.max_position_embeddings, self.head_dim, theta,
@@ -363,7 +381,7 @@ class PagedCausalLM:
     # ------------------------------------------------------------- linear --
     def _linear(self, x, w: Weight, bias=None, residual=None):
         if isinstance(w, QuantizedWeight):
-            return w8a16_linear(x, w.q, w.scale, bias, residual, workspace=self.lin_ws, q_tiled=w.tiled())
+            return w.linear(x, bias, residual, workspace=self.lin_ws)
         return linear16(x, w, bias, residual, workspace=self.lin_ws)
 
     # -------------------------------------------------------------- steps --

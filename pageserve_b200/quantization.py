@@ -82,6 +82,20 @@ def tile_int8_weight(q: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def untile_int8_weight(tiled: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """Inverse of :func:`tile_int8_weight`: the row-major [N][K] int8 weight
+    from the 8 KB-block layout, where 16-byte chunk c of row r of a block is
+    stored at chunk slot c ^ ((r >> 1) & 3). Plain tensor indexing (any
+    device); the model keeps only the tiled copy and rebuilds the row-major
+    one when a caller asks for ``QuantizedWeight.q``."""
+    nb, kt = (N + 127) // 128, (K + 63) // 64
+    t = tiled.view(nb, kt, 128, 4, 16)
+    r = torch.arange(128, device=tiled.device).view(128, 1)
+    c = torch.arange(4, device=tiled.device).view(1, 4)
+    blocks = t[:, :, r, c ^ ((r >> 1) & 3)]  # [nb][kt][128][4][16], chunks back in order
+    return blocks.permute(0, 2, 1, 3, 4).reshape(nb * 128, kt * 64)[:N, :K].contiguous()
+
+
 def w8a16_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None = None,
                  residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
                  workspace: LinearWorkspace | None = None, q_tiled: torch.Tensor | None = None) -> torch.Tensor:
@@ -168,9 +182,8 @@ def linear_swiglu(x: torch.Tensor, weight, out: torch.Tensor | None = None) -> t
     _lib.require_cuda(x)
     lib = _lib.load()
     if isinstance(weight, QuantizedWeight):
-        N2, K = weight.q.shape
-        w_ptr, wdt, wt_ptr, sc_ptr = weight.q.data_ptr(), _lib.PS_I8, weight.tiled().data_ptr(), \
-            weight.scale.data_ptr()
+        N2, K = weight.shape  # int8: the kernels read only the tiled copy
+        w_ptr, wdt, wt_ptr, sc_ptr = None, _lib.PS_I8, weight.tiled().data_ptr(), weight.scale.data_ptr()
     else:
         N2, K = weight.shape
         w_ptr, wdt, wt_ptr, sc_ptr = weight.data_ptr(), _lib.dtype_code(weight.dtype), None, None
@@ -186,7 +199,16 @@ def linear_swiglu(x: torch.Tensor, weight, out: torch.Tensor | None = None) -> t
 
 class QuantizedWeight:
     """engine/quantization.py:30-50, same attributes; ``linear`` runs the
-    fused W8A16 kernel."""
+    fused W8A16 kernel.
+
+    Storage: the row-major int8 ``q`` and/or the kernels' tiled copy
+    (:meth:`tiled`). :meth:`release_row_major` keeps only the tiled copy
+    (one int8 copy of the weight in HBM); ``q`` is then rebuilt from it on
+    each access (exact, for callers outside the hot path)."""
+
+    _q = None
+    _tiled = None
+    _shape = (0, 0)
 
     def __init__(self, weight: torch.Tensor):
         self.dtype = weight.dtype
@@ -200,31 +222,96 @@ class QuantizedWeight:
         obj.scale = scale.reshape(-1, 1).to(torch.float32).contiguous()
         return obj
 
+    @property
+    def q(self) -> torch.Tensor:
+        if self._q is not None:
+            return self._q
+        return untile_int8_weight(self._tiled, *self._shape)
+
+    @q.setter
+    def q(self, value: torch.Tensor) -> None:
+        self._q = value
+        self._shape = tuple(value.shape)
+        self._tiled = None
+
+    def release_row_major(self) -> None:
+        """Keep only the tiled copy (built first if needed)."""
+        self.tiled()
+        self._q = None
+
     def get(self) -> torch.Tensor:
         return dequantize(self.q, self.scale, self.dtype)
 
     def to(self, device) -> "QuantizedWeight":
-        self.q = self.q.to(device)
+        if self._q is not None:
+            self.q = self._q.to(device)
+        else:
+            self._tiled = self._tiled.to(device)
         self.scale = self.scale.to(device)
         return self
 
     @property
     def storage_bytes(self) -> int:
-        return self.q.numel() * self.q.element_size() + self.scale.numel() * self.scale.element_size()
+        """Bytes of the int8 weight and its scales (the reference's count)."""
+        n, k = self._shape
+        return n * k + self.scale.numel() * self.scale.element_size()
 
     @property
     def shape(self) -> tuple[int, int]:
-        return tuple(self.q.shape)
+        return tuple(self._shape)
 
     def tiled(self) -> torch.Tensor:
         """The kernel-side 8 KB-block copy of ``q`` (built once, cached)."""
-        t = getattr(self, "_tiled", None)
-        if t is None or t.device != self.q.device:
-            t = tile_int8_weight(self.q)
+        t = self._tiled
+        if t is None or (self._q is not None and t.device != self._q.device):
+            t = tile_int8_weight(self._q)
             self._tiled = t
         return t
 
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
                out: torch.Tensor | None = None, workspace: LinearWorkspace | None = None) -> torch.Tensor:
-        qt = self.tiled() if x.dtype in (torch.bfloat16, torch.float16) else None
-        return w8a16_linear(x, self.q, self.scale, bias, residual, out, workspace, q_tiled=qt)
+        if x.dtype in (torch.bfloat16, torch.float16):
+            _lib.require_cuda(x, self.scale, bias, residual)
+            return _w8a16_tiled(x, self.tiled(), self.scale, *self._shape, bias, residual, out, workspace)
+        return w8a16_linear(x, self.q, self.scale, bias, residual, out, workspace)
+
+
+class RowView(QuantizedWeight):
+    """Rows ``rows`` (a slice, step 1 or 2) of another QuantizedWeight: the
+    reference-facing per-projection weights of a model whose fused q|k|v and
+    gate|up weights hold the data. ``q`` and ``get()`` read through to the
+    source; :meth:`tiled` is a view of the source's tiled copy when the rows
+    are whole 128-row blocks, else a tiled copy of its own."""
+
+    def __init__(self, src: QuantizedWeight, rows: slice, dtype: torch.dtype):
+        self.dtype = dtype
+        self._src = src
+        self._rows = rows
+        self.scale = src.scale[rows].contiguous()
+        self._shape = (len(range(*rows.indices(src.shape[0]))), src.shape[1])
+
+    @property
+    def q(self) -> torch.Tensor:
+        if self._q is not None:
+            return self._q
+        return self._src.q[self._rows].contiguous()
+
+    @q.setter
+    def q(self, value: torch.Tensor) -> None:  # an explicit assignment detaches the view
+        self._q = value
+        self._shape = tuple(value.shape)
+        self._tiled = None
+
+    def tiled(self) -> torch.Tensor:
+        if self._q is None:
+            start, stop, step = self._rows.indices(self._src.shape[0])
+            N, K = self._src.shape
+            if step == 1 and start % 128 == 0 and (stop % 128 == 0 or stop == N):
+                blk = ((K + 63) // 64) * 8192
+                return self._src.tiled()[(start // 128) * blk:((stop + 127) // 128) * blk]
+        if self._tiled is None:
+            self._tiled = tile_int8_weight(self.q)
+        return self._tiled
+
+    def to(self, device) -> "QuantizedWeight":
+        return QuantizedWeight.from_quantized(self.q.to(device), self.scale.to(device), self.dtype)
