@@ -117,11 +117,16 @@ PS_API int ps_paged_attention(void* out_dev, const void* q_dev, const void* k_ca
  * Same inputs, outputs and semantics as ps_paged_attention, without the
  * workspace arguments: the split-context scratch is a static device array of
  * PS_ATTN_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU loading this library
- * holds until exit. A batch whose scratch need exceeds it is rejected with
- * PS_ERR_INVALID before any launch. The first call on a device looks up the
- * array's address (cudaGetSymbolAddress); make it before any stream capture.
- * Calls that overlap on the GPU share the array and race. Device-side range
- * errors skip the access but are not recorded in the status word. */
+ * holds until exit. A decode batch whose split partials exceed it is
+ * rejected with PS_ERR_INVALID before any launch; a prefill batch (max_q_len x
+ * q heads per kv head > 16) instead splits its key range into fewer pieces,
+ * as many as fit. The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress) and keeps it for the life of the process; make it
+ * before any stream capture, and reload the library after a device reset
+ * (cudaDeviceReset), which may move the array. Calls that overlap on the GPU
+ * share the array and race. This variant owns no status word: device-side
+ * range errors (skipped accesses) and bounded-wait timeouts in the kernels go
+ * unreported, so a caller that needs them uses ps_paged_attention. */
 #define PS_ATTN_NOALLOC_SCRATCH_BYTES (8u << 20)
 PS_API int ps_paged_attention_noalloc(void* out_dev, const void* q_dev, const void* k_cache_dev,
                                       const void* v_cache_dev, const int32_t* block_tables_dev,

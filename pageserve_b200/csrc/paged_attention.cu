@@ -1596,14 +1596,19 @@ int ps_paged_attention(void* out, const void* q, const void* k_cache, const void
 //
 // Its first call on a device looks up the array's device address with
 // cudaGetSymbolAddress (the host-side name of a __device__ array is not a
-// device address); make that first call before any stream capture. All calls
+// device address) and caches it per device for the life of the process; make
+// that first call before any stream capture, and reload the library after a
+// cudaDeviceReset, which may move the array. Decode batches whose partials do
+// not fit are rejected; prefill batches split into as many key pieces as fit
+// (plan_splits' max_ws). All calls
 // on a device share the array: calls that overlap on the GPU (different
 // streams, or threads racing) corrupt each other's partials. Nothing in the
 // array must start at zero: every split writes its partial output and
 // log-sum-exp before the combine kernel reads them, so a previous call's
 // contents are never read. Device-side range errors (a block id outside the
-// pool) skip the access as in ps_paged_attention but are not recorded, since
-// this variant owns no status word.
+// pool) skip the access as in ps_paged_attention, and the kernels' bounded
+// waits still end, but neither is recorded, since this variant owns no status
+// word.
 namespace {
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[PS_ATTN_NOALLOC_SCRATCH_BYTES];
