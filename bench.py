@@ -37,6 +37,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -102,11 +103,12 @@ class Clocks:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        fd, name = tempfile.mkstemp(prefix=f"ps_clocks_{gpu_index}_", suffix=".csv")
+        os.close(fd)
+        self.path = Path(name)
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
@@ -143,6 +145,10 @@ class Clocks:
                         reasons.add(n)
             except (ValueError, IndexError):
                 continue
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
 

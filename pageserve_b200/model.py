@@ -164,6 +164,13 @@ def _one_copy(lw: "LayerWeights", fl: "FusedLayer", dtype) -> None:
         lw.up_w = RowView(fl.gate_up, slice(1, None, 2), dtype)
 
 
+def _check_device_dtype(device, dtype) -> None:
+    if torch.device(device).type != "cuda":
+        raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback); pass device='cuda'")
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"pageserve_b200.PagedCausalLM computes in bfloat16 or float16, not {dtype}")
+
+
 class StepMeta:
     """Device-resident metadata of one step (int32)."""
 
@@ -179,12 +186,19 @@ class StepMeta:
 class PagedCausalLM:
     """engine/model.py:73-193 on the sm_100a kernels."""
 
-    def __init__(self, model_id: str, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
+    def __init__(self, model_id: str, device: str = "cpu", dtype: torch.dtype = torch.float32,
                  quantize: bool = False):
+        """engine/model.py:77-141, same arguments and defaults. This build runs
+        on CUDA only, in bfloat16 or float16: the reference's CPU / float32
+        defaults raise RuntimeError / ValueError (no CPU fallback), so a caller
+        passes ``device="cuda", dtype=torch.bfloat16`` as the reference's own
+        GPU callers do (server.py:40, app.py:80). Like the reference, the
+        checkpoint is loaded in ``dtype`` and quantized from it."""
         from transformers import AutoConfig, AutoModelForCausalLM
 
+        _check_device_dtype(device, dtype)
         config = AutoConfig.from_pretrained(model_id)
-        hf = AutoModelForCausalLM.from_pretrained(model_id, torch_dtype=torch.float32)
+        hf = AutoModelForCausalLM.from_pretrained(model_id, torch_dtype=dtype)
         sd = hf.state_dict()
         del hf
         rope_params = getattr(config, "rope_parameters", None)
@@ -216,9 +230,8 @@ class PagedCausalLM:
         return obj
 
     def _init(self, config, sd, device, dtype, quantize, theta, tp=None, tp_comm="auto", tp_max_tokens=4096):
+        _check_device_dtype(device, dtype)
         self.device = torch.device(device)
-        if self.device.type != "cuda":
-            raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback)")
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         _lib.load()

@@ -292,8 +292,18 @@ class RowView(QuantizedWeight):
 
     @property
     def q(self) -> torch.Tensor:
+        """The view's rows, row-major (rebuilt on each access, outside the hot
+        path): a step-1 view untiles only the 128-row blocks it covers."""
         if self._q is not None:
             return self._q
+        start, stop, step = self._rows.indices(self._src.shape[0])
+        src_tiled = self._src._tiled
+        if step == 1 and self._src._q is None and src_tiled is not None:
+            N, K = self._src.shape
+            b0, b1 = start // 128, (stop + 127) // 128
+            blk = ((K + 63) // 64) * 8192
+            rows = untile_int8_weight(src_tiled[b0 * blk:b1 * blk], (b1 - b0) * 128, K)
+            return rows[start - b0 * 128:stop - b0 * 128].contiguous()
         return self._src.q[self._rows].contiguous()
 
     @q.setter
@@ -303,14 +313,20 @@ class RowView(QuantizedWeight):
         self._tiled = None
 
     def tiled(self) -> torch.Tensor:
+        """A view of the source's tiled copy when the rows are whole 128-row
+        blocks; otherwise a temporary tiled copy, rebuilt on every call and
+        never cached, so the model keeps one int8 copy of each weight (such
+        views, e.g. the step-2 gate/up rows, are slow paths for callers
+        outside the hot path)."""
         if self._q is None:
             start, stop, step = self._rows.indices(self._src.shape[0])
             N, K = self._src.shape
             if step == 1 and start % 128 == 0 and (stop % 128 == 0 or stop == N):
                 blk = ((K + 63) // 64) * 8192
                 return self._src.tiled()[(start // 128) * blk:((stop + 127) // 128) * blk]
+            return tile_int8_weight(self.q)
         if self._tiled is None:
-            self._tiled = tile_int8_weight(self.q)
+            self._tiled = tile_int8_weight(self._q)
         return self._tiled
 
     def to(self, device) -> "QuantizedWeight":
