@@ -79,3 +79,46 @@ def cfg1_inputs(vocab: int = 151936):
         tables.append(ids[at:at + n])
         at += n
     return prompts, tables
+
+
+# Greedy decode fixtures (make_golden.make_greedy): name -> (shape, seed,
+# perturb norms/biases, prompt lengths). "cfg1" is BASELINE config 1's model
+# (Qwen2.5-0.5B shape, all 24 layers, HF init); "3b4" has the Qwen2.5-3B
+# dimensions (hidden 2048, 16/2 heads, head_dim 128, intermediate 11008,
+# vocab 151936) with 4 layers and randomised norms/biases.
+GREEDY_STEPS = 32          # decode steps after the prefill (33 greedy decisions)
+GREEDY_STRIDE = 149        # logits sample stride
+GREEDY_POOL = 256          # KV pool blocks (block size 16)
+
+
+def _greedy_cases():
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent.parent))
+    from pageserve_b200 import synthetic
+    return {
+        "cfg1": (synthetic.QWEN25_0_5B, 0, False, CFG1_CTX),
+        "3b4": (synthetic.QWEN25_3B.with_layers(4), 1, True, (45, 300, 777, 1200)),
+    }
+
+
+GREEDY_CASES = _greedy_cases()
+
+
+def greedy_inputs(name: str):
+    """Prompts and block tables of a greedy fixture: seeded random token ids;
+    each sequence's table is a consecutive slice of a random.Random(17)
+    permutation of the GREEDY_POOL-block pool, long enough for prompt +
+    GREEDY_STEPS + 1 tokens."""
+    shape, seed, _, ctxs = GREEDY_CASES[name]
+    rng = np.random.default_rng(1000 + seed)
+    prompts = [rng.integers(0, shape.vocab, size=c).astype(np.int64) for c in ctxs]
+    ids = list(range(GREEDY_POOL))
+    random.Random(17).shuffle(ids)
+    tables, at = [], 0
+    for c in ctxs:
+        n = (c + GREEDY_STEPS + 1 + 15) // 16
+        tables.append(ids[at:at + n])
+        at += n
+    assert at <= GREEDY_POOL
+    return prompts, tables

@@ -27,6 +27,9 @@ Fixtures:
   model_cfg1.npz           BASELINE config 1: the Qwen2.5-0.5B shape, int8,
                            fp32, 4 sequences at context 37/128/255/511
                            (summaries only: the logits are 4 x 151936)
+  greedy_<name>.npz        greedy decode, 4 sequences x (prefill + 32 decode
+                           steps), float32 and the reference's own bf16 picks
+                           (cases.GREEDY_CASES)
 """
 
 from __future__ import annotations
@@ -264,6 +267,20 @@ def make_cfg1():
         res[f"{i}/k_layer_abs"] = np.abs(kk).astype(np.float64).sum(axis=(1, 2, 3))
         res[f"{i}/k_last_layer_rows"] = kk[-1, ::7]
         res[f"{i}/v_last_layer_rows"] = vv[-1, ::7]
+    # the reference's own bf16 path (its GPU dtype) on the same inputs: its picks
+    with tempfile.TemporaryDirectory() as tmp:
+        sd = synthetic.generate_state_dict(shape, seed=0)
+        _save_checkpoint(shape, sd, tmp)
+        del sd
+        mb = ref_model.PagedCausalLM(tmp, device="cpu", dtype=torch.bfloat16, quantize=True)
+    mb.allocate_kv_cache(256, 16)
+    for i, (p, tab) in enumerate(zip(prompts, tables)):
+        ctx = len(p)
+        with torch.no_grad():
+            lp = mb.forward_step(_t(p[:-1]), tab, 0)
+            ld = mb.forward_step(_t(p[-1:]), tab, ctx - 1)
+        res[f"{i}/prefill/argmax_bf16"] = np.asarray(int(lp[-1].argmax()))
+        res[f"{i}/decode/argmax_bf16"] = np.asarray(int(ld[-1].argmax()))
     for i, (p, tab) in enumerate(zip(prompts, tables)):
         res[f"{i}/tokens"] = p
         res[f"{i}/table"] = np.asarray(tab, np.int32)
@@ -272,10 +289,74 @@ def make_cfg1():
     np.savez_compressed(HERE / "model_cfg1.npz", **res)
 
 
+def make_greedy():
+    """Greedy decode by the reference (engine/model.py:149-193 driven one
+    sequence at a time, as engine/runner.py:65-79 and
+    scripts/verify_end_to_end.py:63-91 do): each sequence prefills its prompt,
+    then takes cases.GREEDY_STEPS decode steps feeding back
+    ``int(logits[-1].argmax())``. Per decision the fixture keeps the chosen
+    token, the reference's top-16 (ids, logits) and a strided sample of the
+    logits, so a test can tell a near-tie flip from a real one. A second run of
+    the reference in bfloat16 (its GPU dtype), fed the float32 run's tokens,
+    records its own pick at every decision (``gen_bf16``)."""
+    for name, (shape, seed, perturb, ctxs) in cases.GREEDY_CASES.items():
+        sd = synthetic.generate_state_dict(shape, seed=seed, perturb_norms_biases=perturb)
+        prompts, tables = cases.greedy_inputs(name)
+        with tempfile.TemporaryDirectory() as tmp:
+            _save_checkpoint(shape, sd, tmp)
+            del sd
+            m = ref_model.PagedCausalLM(tmp, device="cpu", dtype=torch.float32, quantize=True)
+        m.allocate_kv_cache(cases.GREEDY_POOL, 16)
+        S = cases.GREEDY_STEPS + 1
+        gen = np.zeros((len(prompts), S), np.int64)
+        top_idx = np.zeros((len(prompts), S, 16), np.int64)
+        top_val = np.zeros((len(prompts), S, 16), np.float32)
+        samples = []
+        for i, (p, tab) in enumerate(zip(prompts, tables)):
+            rows = []
+            with torch.no_grad():
+                lg = m.forward_step(_t(p), tab, 0)[-1]
+                for t in range(S):
+                    lgn = lg.numpy().astype(np.float32)
+                    order = np.argsort(-lgn, kind="stable")[:16]
+                    tok = int(lg.argmax())
+                    gen[i, t] = tok
+                    top_idx[i, t] = order
+                    top_val[i, t] = lgn[order]
+                    rows.append(lgn[::cases.GREEDY_STRIDE])
+                    if t + 1 < S:
+                        lg = m.forward_step(torch.tensor([tok]), tab, len(p) + t)[-1]
+            samples.append(np.stack(rows))
+            print(f"  {name} seq {i}: ctx {len(p)} -> {gen[i].tolist()}", flush=True)
+        # The reference's own bf16 path on the same decisions (teacher forced
+        # with the float32 run's tokens): its greedy pick at every decision.
+        with tempfile.TemporaryDirectory() as tmp:
+            sd = synthetic.generate_state_dict(shape, seed=seed, perturb_norms_biases=perturb)
+            _save_checkpoint(shape, sd, tmp)
+            del sd
+            mb = ref_model.PagedCausalLM(tmp, device="cpu", dtype=torch.bfloat16, quantize=True)
+        mb.allocate_kv_cache(cases.GREEDY_POOL, 16)
+        gen_bf16 = np.zeros_like(gen)
+        for i, (p, tab) in enumerate(zip(prompts, tables)):
+            with torch.no_grad():
+                lg = mb.forward_step(_t(p), tab, 0)[-1]
+                for t in range(S):
+                    gen_bf16[i, t] = int(lg.argmax())
+                    if t + 1 < S:
+                        lg = mb.forward_step(torch.tensor([int(gen[i, t])]), tab, len(p) + t)[-1]
+            print(f"  {name} seq {i} bf16: {int((gen_bf16[i] != gen[i]).sum())} of {S} decisions differ", flush=True)
+        res = {"gen": gen, "top_idx": top_idx, "top_val": top_val, "sample": np.stack(samples),
+               "stride": np.asarray(cases.GREEDY_STRIDE), "gen_bf16": gen_bf16}
+        for i, (p, tab) in enumerate(zip(prompts, tables)):
+            res[f"{i}/tokens"] = p
+            res[f"{i}/table"] = np.asarray(tab, np.int32)
+        np.savez_compressed(HERE / f"greedy_{name}.npz", **res)
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["attention", "quant", "norm_rope", "tp", "tiny", "cfg1"]
+    which = sys.argv[1:] or ["attention", "quant", "norm_rope", "tp", "tiny", "cfg1", "greedy"]
     for w in which:
         print("generating", w, flush=True)
         {"attention": make_attention, "quant": make_quant, "norm_rope": make_norm_rope, "tp": make_tp,
-         "tiny": make_tiny_model, "cfg1": make_cfg1}[w]()
+         "tiny": make_tiny_model, "cfg1": make_cfg1, "greedy": make_greedy}[w]()
     print("done")

@@ -141,3 +141,25 @@ def test_oracle_config1_matches_reference():
         kk = np.stack([m.k_cache[:, tab[pp // 16], pp % 16] for pp in range(ctx)], axis=1)
         np.testing.assert_allclose(kk.astype(np.float64).sum(axis=(1, 2, 3)), g[f"{i}/k_layer_sum"], atol=5e-2, rtol=1e-5)
         np.testing.assert_allclose(kk[-1, ::7], g[f"{i}/k_last_layer_rows"], atol=5e-4, rtol=0)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name,seq,steps", [("cfg1", 0, 12), ("3b4", 0, 6)])
+def test_oracle_greedy_decode_matches_reference(name, seq, steps):
+    """The reference's greedy decode (tests/golden/greedy_*.npz), teacher
+    forced on the oracle: the same pick at every decision and the same top-16
+    logits (float32 against float32: only summation order differs)."""
+    g = np.load(GOLDEN / f"greedy_{name}.npz")
+    shape, seed, perturb, _ = cases.GREEDY_CASES[name]
+    prompts, tables = cases.greedy_inputs(name)
+    sd = synthetic.generate_state_dict(shape, seed=seed, perturb_norms_biases=perturb)
+    m = OracleCausalLM(sd, shape, quantize=True, max_position=2048)
+    del sd
+    m.allocate_kv_cache(cases.GREEDY_POOL, 16)
+    p, tab = prompts[seq], tables[seq]
+    lg = m.forward_step(p, tab, 0, logits_rows=[len(p) - 1])[-1]
+    for t in range(steps):
+        assert int(lg.argmax()) == int(g["gen"][seq, t]), f"decision {t}"
+        np.testing.assert_allclose(lg[g["top_idx"][seq, t]], g["top_val"][seq, t], atol=2e-4, rtol=0)
+        np.testing.assert_allclose(lg[::int(g["stride"])], g["sample"][seq, t], atol=2e-4, rtol=0)
+        lg = m.forward_step([int(g["gen"][seq, t])], tab, len(p) + t)[-1]
