@@ -59,6 +59,14 @@ def _use_config5():
     N_DECODE, CTX, PREFILL, CONFIG, SHAPE_NAME = 128, 4096, 0, 5, "qwen2.5-32b"
 
 
+TP_COMM_NAMES = {
+    "fused": "fused one-shot peer-memory push (o_proj/down -> next RMSNorm)",
+    "fused2": "fused two-shot: GEMM scatters column slices to owners, owner reduces + all-gathers the residual, "
+              "local RMSNorm",
+    "nccl": "NCCL all_reduce",
+}
+
+
 def _peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -497,8 +505,7 @@ def run_gpu(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random init, random KV contents)",
             "config": _config({"parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
                                else "single GPU",
-                               **({"tp_allreduce": "fused peer-memory push (o_proj/down -> next RMSNorm)"
-                                   if m.tp_comm == "fused" else "NCCL all_reduce"} if tp else {})}),
+                               **({"tp_allreduce": TP_COMM_NAMES[m.tp_comm]} if tp else {})}),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": g.h2d_bytes, "d2h_bytes_per_step": g.d2h_bytes,
                     "api": "StepGraph.run (host ids/metadata in, host next tokens out)"},
             "gpu_launches": launches, "launches_per_step": g.launches_per_replay,
@@ -533,7 +540,7 @@ def main():
     ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
     ap.add_argument("--prefill", type=int, default=None,
                     help="prefill chunk tokens per step (default 512 = BASELINE config 4; 0 = decode-only step)")
-    ap.add_argument("--tp-comm", default="auto", choices=["auto", "fused", "nccl"],
+    ap.add_argument("--tp-comm", default="auto", choices=["auto", "fused", "fused2", "nccl"],
                     help="N>1 tensor parallelism: row-parallel reduction transport")
     ap.add_argument("--config", type=int, default=4, choices=[4, 5],
                     help="BASELINE configuration: 4 = 3B-shape mixed step (default), 5 = 32B-shape TP decode")

@@ -238,11 +238,16 @@ PS_API int ps_linear_swiglu(void* y_dev, const void* x_dev, const void* w_dev, i
  *     counter at 64 + 4*s and its producer CTA counter at 128 + 4*s (local);
  *     a 'broken' word at 192, set by the first wait that times out, makes
  *     every later wait on this buffer give up at once (re-zero to clear);
- *   then slots [2 sets][world][max_tokens][hidden] of dtype.
+ *     from byte 1024, u32 [2 sets][256] row-block counters of the two-shot
+ *     gather;
+ *   then xg [2 sets][max_tokens][hidden] of dtype (the two-shot gathered
+ *     residual stream), padded to 256 bytes;
+ *   then slots [2 sets][world][max_tokens][hidden] of dtype (two-shot:
+ *     [2 sets][world][max_tokens][hidden/world]).
  * The two sets alternate (o_proj -> set 0, down_proj -> set 1). Every wait is
  * bounded (a few seconds); on timeout PS_ERR_TIMEOUT-style code 4 is recorded
  * in the device status word (ps_device_status) and the kernel finishes. */
-#define PS_COMM_CTRL_BYTES 1024
+#define PS_COMM_CTRL_BYTES 4096
 #define PS_COMM_MAX_WORLD 8
 
 PS_API size_t ps_comm_buffer_bytes(int world, int max_tokens, int hidden, int dtype);
@@ -270,6 +275,35 @@ PS_API int ps_linear_push(const void* x_dev, const void* w_dev, int wdtype, cons
                           const float* scale_dev, int M, int N, int K, int dtype, void* const* rank_bufs, int world,
                           int rank, int set, int max_tokens, void* workspace_dev, size_t workspace_bytes,
                           ps_stream_t stream);
+
+/* Two-shot form of ps_linear_push (the reduce-scatter half of the
+ * all-reduce): columns [d * N/world, (d + 1) * N/world) of the (M, N) result
+ * go to rank d only, into its slot [set][rank] of that column slice
+ * ([max_tokens][N/world]); then every rank's flag of `set` is raised by one.
+ * N/world must be a multiple of 128. Each rank sends (world-1)/world of its
+ * partial instead of world-1 copies. Consumed by ps_tp_reduce_rmsnorm. */
+PS_API int ps_linear_push_scatter(const void* x_dev, const void* w_dev, int wdtype, const int8_t* w_tiled_dev,
+                                  const float* scale_dev, int M, int N, int K, int dtype, void* const* rank_bufs,
+                                  int world, int rank, int set, int max_tokens, void* workspace_dev,
+                                  size_t workspace_bytes, ps_stream_t stream);
+
+/* The two-shot consumer (tensor_parallel.py:47 + engine/model.py:184-190):
+ * this rank owns columns [rank * H/world, (rank + 1) * H/world). It waits for
+ * every rank's scatter of `set`, sums the slots of its columns (float32, rank
+ * order, rounded to dtype), adds x_old (the residual stream, row stride H;
+ * NULL: none), stores the new residual slice into the gathered region
+ * xg[set] of every rank's buffer (the all-gather, peer stores), then, once
+ * all ranks' slices of a row block have arrived, writes y = rmsnorm(x) *
+ * weight for whole rows (y = x when weight_dev is NULL). The new residual
+ * stream stays in xg[set] (ps_comm_gathered_offset) for the next reduction's
+ * x_old. phases: 3 (one launch per rank); a process emulating several ranks
+ * on one GPU launches phase 1 for every rank, then phase 2 for every rank. */
+PS_API int ps_tp_reduce_rmsnorm(void* y_dev, const void* x_old_dev, const void* weight_dev, float eps, int M, int H,
+                                int dtype, void* const* rank_bufs, int world, int rank, int set, int max_tokens,
+                                int phases, ps_stream_t stream);
+/* Byte offset of xg[set] (the gathered residual stream, [max_tokens][hidden])
+ * inside a receive buffer; 0 for invalid arguments. */
+PS_API size_t ps_comm_gathered_offset(int world, int max_tokens, int hidden, int dtype, int set);
 
 /* The consumer (tensor_parallel.py:47 + engine/model.py:184-190): waits until
  * `set`'s flag in this rank's buffer shows all `world` ranks, s = sum over

@@ -64,6 +64,9 @@ _SIGNATURES = {
     "ps_ipc_close": (c_int, [_P]),
     "ps_linear_push": (c_int, [_P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _I, _I, _I, _P, c_size_t, _P]),
     "ps_allreduce_rmsnorm": (c_int, [_P, _P, _P, c_float, _I, _I, _I, _P, _I, _I, _I, _P]),
+    "ps_linear_push_scatter": (c_int, [_P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _I, _I, _I, _P, c_size_t, _P]),
+    "ps_tp_reduce_rmsnorm": (c_int, [_P, _P, _P, c_float, _I, _I, _I, _P, _I, _I, _I, _I, _I, _P]),
+    "ps_comm_gathered_offset": (c_size_t, [_I, _I, _I, _I, _I]),
 }
 
 _lock = threading.Lock()
@@ -90,6 +93,24 @@ def load() -> ctypes.CDLL:
                 fn.argtypes = args
             _lib = lib
     return _lib
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over raw device memory this library owns."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3}
+
+
+def device_view(ptr: int, shape: tuple, dtype, device) -> "object":
+    """A torch tensor viewing device memory at ``ptr`` (no copy; the memory
+    must outlive the view). 16-bit dtypes are viewed through int16."""
+    import torch
+    n = 1
+    for d in shape:
+        n *= d
+    raw = torch.as_tensor(_DeviceArray(ptr, (n,), "<i2"), device=device)
+    return raw.view(dtype).view(*shape)
 
 
 def exported_symbols() -> list[str]:

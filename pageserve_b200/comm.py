@@ -18,6 +18,14 @@ The two slot sets alternate between the o_proj (set 0) and down_proj
 ranks' buffers in one process on one GPU (every rank's kernels issued in
 sequence on one stream), which exercises the same kernels and flags
 without a second GPU.
+
+Two-shot form (``linear_push(..., scatter=True)`` + ``reduce_norm``): the
+linear sends each column slice of its output only to the rank that owns it
+(reduce-scatter); the owner sums its slice, adds the residual, and stores the
+new residual slice into every rank's gathered region (all-gather), where each
+rank normalises whole rows. Per rank that moves 2 (W-1)/W of the output over
+NVLink instead of the one-shot's W-1 copies; the residual stream then lives
+in the gathered region of the set (``gathered_ptr``).
 """
 
 from __future__ import annotations
@@ -119,10 +127,11 @@ class FusedAllReduce:
             lib.ps_comm_free(p)
 
     # --------------------------------------------------------- kernels ----
-    def linear_push(self, x: torch.Tensor, weight, set_: int, workspace=None) -> None:
+    def linear_push(self, x: torch.Tensor, weight, set_: int, workspace=None, scatter: bool = False) -> None:
         """Row-parallel local product of this rank (x (M, K_shard) @ W.T), pushed
-        to every rank's slot ``set_``. ``weight``: QuantizedWeight (int8,
-        per-row scale) or a bf16/f16 tensor (N, K_shard)."""
+        to every rank's slot ``set_`` (``scatter``: only each rank's column
+        slice, to that rank). ``weight``: QuantizedWeight (int8, per-row scale)
+        or a bf16/f16 tensor (N, K_shard)."""
         from .quantization import LinearWorkspace, QuantizedWeight, _default_ws
         _lib.require_cuda(x)
         M, K = x.shape
@@ -141,9 +150,47 @@ class FusedAllReduce:
         if workspace is None:
             workspace = _default_ws.setdefault(x.device, LinearWorkspace())
         buf = workspace.get(ws_bytes, x.device)
-        _lib.check(lib.ps_linear_push(x.data_ptr(), w_ptr, wdt, wt_ptr, sc_ptr, M, N, K, _lib.dtype_code(x.dtype),
-                                      self._rank_bufs, self.world, self.rank, set_, self.max_tokens, _lib.ptr(buf),
-                                      ws_bytes, _lib.stream_ptr(x.device)), "linear_push")
+        fn = lib.ps_linear_push_scatter if scatter else lib.ps_linear_push
+        _lib.check(fn(x.data_ptr(), w_ptr, wdt, wt_ptr, sc_ptr, M, N, K, _lib.dtype_code(x.dtype), self._rank_bufs,
+                      self.world, self.rank, set_, self.max_tokens, _lib.ptr(buf), ws_bytes,
+                      _lib.stream_ptr(x.device)), "linear_push")
+
+    def linear_push_scatter(self, x: torch.Tensor, weight, set_: int, workspace=None) -> None:
+        """Two-shot producer: like :meth:`linear_push`, but each rank receives
+        only its own column slice of the output."""
+        self.linear_push(x, weight, set_, workspace, scatter=True)
+
+    def gathered_ptr(self, set_: int) -> int:
+        """Device address of this rank's gathered residual stream of ``set_``
+        ([max_tokens][hidden]; written by ``reduce_norm``)."""
+        off = _lib.load().ps_comm_gathered_offset(self.world, self.max_tokens, self.hidden,
+                                                  _lib.dtype_code(self.dtype), set_)
+        if off == 0:
+            raise ValueError("invalid gathered region")
+        return self.buf + off
+
+    def gathered(self, set_: int, M: int) -> torch.Tensor:
+        """View of the first ``M`` rows of the gathered residual stream of
+        ``set_`` (valid until that set's next reduction)."""
+        return _lib.device_view(self.gathered_ptr(set_), (M, self.hidden), self.dtype, self.device)
+
+    def reduce_norm(self, x_old: int | torch.Tensor | None, weight: torch.Tensor | None, eps: float, set_: int,
+                    M: int, out: torch.Tensor | None = None, phases: int = 3) -> torch.Tensor:
+        """Two-shot consumer of ``set_``: the residual stream becomes
+        x_old + the reduced sum (left in ``gathered_ptr(set_)``), and the
+        return value is rmsnorm(x) * weight for all M rows (x itself when
+        ``weight`` is None). ``x_old``: a (M, hidden) tensor, a device
+        address with row stride hidden, or None."""
+        if out is None:
+            out = torch.empty((M, self.hidden), dtype=self.dtype, device=self.device)
+        xo = x_old.data_ptr() if isinstance(x_old, torch.Tensor) else x_old
+        if weight is not None:
+            _lib.require_cuda(weight)
+        _lib.check(_lib.load().ps_tp_reduce_rmsnorm(out.data_ptr(), xo, _lib.ptr(weight), float(eps), M, self.hidden,
+                                                     _lib.dtype_code(self.dtype), self._rank_bufs, self.world,
+                                                     self.rank, set_, self.max_tokens, phases,
+                                                     _lib.stream_ptr(self.device)), "tp_reduce_rmsnorm")
+        return out
 
     def allreduce_rmsnorm(self, x: torch.Tensor | None, weight: torch.Tensor | None, eps: float, set_: int,
                           M: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:

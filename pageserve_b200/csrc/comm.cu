@@ -51,7 +51,7 @@ template <typename T, int MAXV, bool NORM>
 __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(T* __restrict__ y, T* __restrict__ x,
                                                                 const T* __restrict__ w, float eps, int M, int H,
                                                                 void* buf, int W, int set, long long slot_elems,
-                                                                int* status) {
+                                                                long long slots_off, int* status) {
   pdl_wait();
   pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(T* __restrict__ 
     }
   }
   __syncthreads();
-  const T* slots = reinterpret_cast<const T*>(static_cast<const unsigned char*>(buf) + PS_COMM_CTRL_BYTES) +
+  const T* slots = reinterpret_cast<const T*>(static_cast<const unsigned char*>(buf) + slots_off) +
                    static_cast<long long>(set) * W * slot_elems;
   const int row = blockIdx.x;
   const long long roff = static_cast<long long>(row) * H;
@@ -146,6 +146,148 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(T* __restrict__ 
   }
 }
 
+struct RankBufs {
+  void* b[kMaxWorld];  // every rank's receive buffer, as mapped in this process
+};
+
+PS_DEVICE bool wait_count(const unsigned* p, unsigned target, void* buf, int* status) {
+  const long long t0 = clock64();
+  volatile unsigned* broken = ctrl_broken(buf);
+  while (ld_acquire_sys(p) < target) {
+    if (*broken) {
+      record_error(status, kErrTimeout);
+      return false;
+    }
+    if (clock64() - t0 > kCommWaitCycles) {
+      *broken = 1u;
+      record_error(status, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Two-shot consumer: the rest of the all-reduce after a scattering
+// row-parallel linear, plus the residual add and RMSNorm (engine/
+// tensor_parallel.py:47, engine/model.py:184-190). Rank `rank` owns the
+// columns [rank * S, (rank + 1) * S), S = H / W; CTA b owns rows
+// [b * R, (b + 1) * R).
+// Phase 1: wait until the set's flag shows W scatters; for the CTA's rows and
+//   the owned columns, x = T(x_old + T(sum of the W slots, rank order));
+//   store x into xg[set] of EVERY rank (the all-gather, 16-byte stores, peers
+//   over NVLink), then count the row block on every rank. The last CTA to
+//   finish re-arms the set's flag.
+// Phase 2: wait until this rank's count of the row block shows W, re-arm it,
+//   and normalise whole rows read from xg[set]: y = rmsnorm(x) * w (y = x
+//   without a weight).
+// `phases` is 3 for real ranks; one process emulating several ranks on one
+// GPU runs phase 1 of every rank before phase 2 of any (nothing then waits
+// on a later launch). x_old (row stride H) is the residual stream the
+// previous reduction gathered (xg of the other set), or the embedding output.
+template <typename T>
+__global__ void __launch_bounds__(256) tp_reduce_rmsnorm_kernel(T* __restrict__ y, const T* __restrict__ x_old,
+                                                                const T* __restrict__ w, float eps, int M, int H,
+                                                                RankBufs bufs, int W, int rank, int set,
+                                                                int max_tokens, int R, int phases,
+                                                                long long xg_off, long long slots_off, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int VEC = 16 / sizeof(T);
+  void* own = bufs.b[rank];
+  const int S = H / W;
+  const int m0 = blockIdx.x * R;
+  const int rows = min(R, M - m0);
+  unsigned* gcount = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(own) + kGatherCountOff) +
+                     set * kGatherBlocks + blockIdx.x;
+  const long long xg_set = static_cast<long long>(set) * max_tokens * H;  // elements
+  if (phases & 1) {
+    unsigned* flag = ctrl_flag(own, set);
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = wait_count(flag, static_cast<unsigned>(W), own, status) ? 1 : 0;
+    __syncthreads();
+    const T* slots = reinterpret_cast<const T*>(static_cast<const unsigned char*>(own) + slots_off) +
+                     static_cast<long long>(set) * W * max_tokens * S;
+    const int vpr = S / VEC;  // 16-byte vectors per row of the slice
+    for (int i = threadIdx.x; i < rows * vpr && ok; i += blockDim.x) {
+      const int m = m0 + i / vpr;
+      const int c = (i % vpr) * VEC;  // column within the slice
+      float acc[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+      for (int r = 0; r < W; ++r) {  // rank order: the same sum on every run
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(slots + (static_cast<long long>(r) * max_tokens + m) * S + c));
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] += to_f32(e[k]);
+      }
+      const long long col = static_cast<long long>(rank) * S + c;
+      if (x_old) {
+        float xo[VEC];
+        unpack8<T>(*reinterpret_cast<const uint4*>(x_old + static_cast<long long>(m) * H + col), xo);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] = xo[k] + to_f32(from_f32<T>(acc[k]));
+      }
+      const uint4 pk = pack8<T>(acc);
+      const long long off = xg_set + static_cast<long long>(m) * H + col;
+      for (int r = 0; r < W; ++r) {
+        T* xg = reinterpret_cast<T*>(static_cast<unsigned char*>(bufs.b[r]) + xg_off);
+        *reinterpret_cast<uint4*>(xg + off) = pk;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // this CTA's stores (ordered by the barrier) before the counts
+      for (int r = 0; r < W; ++r) {
+        unsigned* g = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(bufs.b[r]) + kGatherCountOff) +
+                      set * kGatherBlocks + blockIdx.x;
+        red_release_sys_add(g, 1u);
+      }
+      // re-arm the flag once every CTA has seen it
+      unsigned* consumed = ctrl_consumed(own, set);
+      const unsigned prev = atomicAdd(consumed, 1u);
+      if (prev == gridDim.x - 1) {
+        atomicExch(consumed, 0u);
+        atomicExch(flag, 0u);
+        __threadfence_system();
+      }
+    }
+  }
+  if (phases & 2) {
+    __shared__ int ok2;
+    if (threadIdx.x == 0) {
+      ok2 = wait_count(gcount, static_cast<unsigned>(W), own, status) ? 1 : 0;
+      if (ok2) atomicExch(gcount, 0u);  // only this CTA reads this count; every rank's W adds have landed
+    }
+    __syncthreads();
+    if (!ok2) return;
+    const T* xg = reinterpret_cast<const T*>(static_cast<const unsigned char*>(own) + xg_off) + xg_set;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nvec = H / VEC;
+    for (int r = warp; r < rows; r += blockDim.x / 32) {
+      const long long ro = static_cast<long long>(m0 + r) * H;
+      float ss = 0.f;
+      for (int c = lane; c < nvec; c += 32) {  // pass 1: sum of squares (written by peers: L2 loads)
+        float v[VEC];
+        unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(xg + ro) + c), v);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) ss += v[k] * v[k];
+      }
+      ss = warp_sum(ss);
+      const float inv = w ? rsqrtf(ss / static_cast<float>(H) + eps) : 1.f;
+      for (int c = lane; c < nvec; c += 32) {
+        float v[VEC], wv[VEC];
+        unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(xg + ro) + c), v);
+        if (w) {
+          unpack8<T>(reinterpret_cast<const uint4*>(w)[c], wv);
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) v[k] = v[k] * inv * wv[k];
+        }
+        reinterpret_cast<uint4*>(y + ro)[c] = pack8<T>(v);
+      }
+    }
+  }
+}
+
 int elem_bytes(int dtype) { return dtype == PS_BF16 || dtype == PS_F16 ? 2 : 0; }
 
 }  // namespace
@@ -153,22 +295,28 @@ int elem_bytes(int dtype) { return dtype == PS_BF16 || dtype == PS_F16 ? 2 : 0; 
 namespace ps_host {
 
 int push_targets(ps::PushTargets* pt, void* const* rank_bufs, int world, int rank, int set, int max_tokens, int n,
-                 int esize) {
+                 int esize, bool scatter) {
   if (!rank_bufs || world < 1 || world > ps::kMaxWorld || rank < 0 || rank >= world || (set != 0 && set != 1) ||
       max_tokens < 1 || n < 1 || esize < 1) {
     set_error("linear_push: invalid world/rank/set/max_tokens");
     return PS_ERR_INVALID;
   }
+  if (scatter && (n % world != 0 || (n / world) % 128 != 0)) {
+    set_error("linear_push: two-shot needs N (%d) split into %d slices of whole 128-column tiles", n, world);
+    return PS_ERR_UNSUPPORTED;
+  }
   std::memset(pt, 0, sizeof(*pt));
   pt->world = world;
-  const long long slot_bytes = static_cast<long long>(max_tokens) * n * esize;
+  pt->slice = scatter ? n / world : 0;
+  const ps::CommLayout lay = ps::comm_layout(world, max_tokens, n, esize);
+  const long long slot_bytes = static_cast<long long>(max_tokens) * (scatter ? n / world : n) * esize;
   for (int r = 0; r < world; ++r) {
     unsigned char* b = static_cast<unsigned char*>(rank_bufs[r]);
     if (!b || !aligned(b, 256)) {
       set_error("linear_push: receive buffer of rank %d is null or not 256-byte aligned", r);
       return PS_ERR_INVALID;
     }
-    pt->dst[r] = b + PS_COMM_CTRL_BYTES + (static_cast<long long>(set) * world + rank) * slot_bytes;
+    pt->dst[r] = b + lay.slots + (static_cast<long long>(set) * world + rank) * slot_bytes;
     pt->flag[r] = reinterpret_cast<unsigned*>(b) + set;
   }
   pt->arrivals = reinterpret_cast<unsigned*>(rank_bufs[rank]) + 32 + set;
@@ -183,7 +331,7 @@ extern "C" {
 PS_API size_t ps_comm_buffer_bytes(int world, int max_tokens, int hidden, int dtype) {
   const int es = elem_bytes(dtype);
   if (world < 1 || world > ps::kMaxWorld || max_tokens < 1 || hidden < 1 || es == 0) return 0;
-  return PS_COMM_CTRL_BYTES + 2ull * world * max_tokens * hidden * es;
+  return static_cast<size_t>(ps::comm_layout(world, max_tokens, hidden, es).total);
 }
 
 PS_API int ps_comm_alloc(void** buf, size_t bytes) {
@@ -287,12 +435,13 @@ PS_API int ps_allreduce_rmsnorm(void* y, void* x, const void* weight, float eps,
     return PS_ERR_UNSUPPORTED;
   }
   const long long slot = static_cast<long long>(max_tokens) * H;
+  const long long slots_off = ps::comm_layout(world, max_tokens, H, 2).slots;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int* st = ps_host::status_word(PS_TU_COMM);
 #define PS_ARN(T, MV, NORM)                                                                                   \
   ps_host::launch(allreduce_rmsnorm_kernel<T, MV, NORM>, M, 256, 0, s, static_cast<T*>(y), static_cast<T*>(x),            \
                                                           static_cast<const T*>(weight), eps, M, H, buf, world, \
-                                                          set, slot, st)
+                                                          set, slot, slots_off, st)
 #define PS_ARN_N(T, MV) \
   if (norm) PS_ARN(T, MV, true); else PS_ARN(T, MV, false)
 #define PS_ARN_T(T)                   \
@@ -312,6 +461,69 @@ PS_API int ps_allreduce_rmsnorm(void* y, void* x, const void* weight, float eps,
 #undef PS_ARN
   ps_host::count_launch();
   return ps_host::check_launch("allreduce_rmsnorm");
+}
+
+PS_API int ps_tp_reduce_rmsnorm(void* y, const void* x_old, const void* weight, float eps, int M, int H, int dtype,
+                                void* const* rank_bufs, int world, int rank, int set, int max_tokens, int phases,
+                                ps_stream_t stream) {
+  if (M <= 0 || H <= 0 || world < 1 || world > ps::kMaxWorld || rank < 0 || rank >= world || M > max_tokens ||
+      (set != 0 && set != 1) || phases < 1 || phases > 3 || !y || !rank_bufs) {
+    ps_host::set_error("tp_reduce_rmsnorm: invalid arguments (M=%d H=%d world=%d rank=%d set=%d max_tokens=%d)", M,
+                       H, world, rank, set, max_tokens);
+    return PS_ERR_INVALID;
+  }
+  if (H % world != 0 || (H / world) % 8 != 0) {
+    ps_host::set_error("tp_reduce_rmsnorm: hidden %d must split into %d slices of whole 16-byte vectors", H, world);
+    return PS_ERR_UNSUPPORTED;
+  }
+  if (!ps_host::aligned(y, 16) || !ps_host::aligned(x_old, 16) || !ps_host::aligned(weight, 16)) {
+    ps_host::set_error("tp_reduce_rmsnorm: tensors must be 16-byte aligned");
+    return PS_ERR_INVALID;
+  }
+  RankBufs rb;
+  std::memset(&rb, 0, sizeof(rb));
+  for (int r = 0; r < world; ++r) {
+    if (!rank_bufs[r] || !ps_host::aligned(rank_bufs[r], 256)) {
+      ps_host::set_error("tp_reduce_rmsnorm: receive buffer of rank %d is null or not 256-byte aligned", r);
+      return PS_ERR_INVALID;
+    }
+    rb.b[r] = rank_bufs[r];
+  }
+  const ps::CommLayout lay = ps::comm_layout(world, max_tokens, H, 2);
+  // rows per CTA: about one CTA per SM, at most kGatherBlocks CTAs (the counters)
+  int R = (M + 147) / 148;
+  if (R < 1) R = 1;
+  const int grid = (M + R - 1) / R;
+  if (grid > ps::kGatherBlocks) {
+    ps_host::set_error("tp_reduce_rmsnorm: %d row blocks exceed %d", grid, ps::kGatherBlocks);
+    return PS_ERR_UNSUPPORTED;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int* st = ps_host::status_word(PS_TU_COMM);
+  if (dtype == PS_BF16) {
+    using T = __nv_bfloat16;
+    ps_host::launch(tp_reduce_rmsnorm_kernel<T>, grid, 256, 0, s, static_cast<T*>(y), static_cast<const T*>(x_old),
+                    static_cast<const T*>(weight), eps, M, H, rb, world, rank, set, max_tokens, R, phases, lay.xg,
+                    lay.slots, st);
+  } else if (dtype == PS_F16) {
+    using T = __half;
+    ps_host::launch(tp_reduce_rmsnorm_kernel<T>, grid, 256, 0, s, static_cast<T*>(y), static_cast<const T*>(x_old),
+                    static_cast<const T*>(weight), eps, M, H, rb, world, rank, set, max_tokens, R, phases, lay.xg,
+                    lay.slots, st);
+  } else {
+    ps_host::set_error("tp_reduce_rmsnorm: dtype must be bf16 or f16");
+    return PS_ERR_UNSUPPORTED;
+  }
+  ps_host::count_launch();
+  return ps_host::check_launch("tp_reduce_rmsnorm");
+}
+
+PS_API size_t ps_comm_gathered_offset(int world, int max_tokens, int hidden, int dtype, int set) {
+  const int es = elem_bytes(dtype);
+  if (world < 1 || world > ps::kMaxWorld || max_tokens < 1 || hidden < 1 || es == 0 || (set != 0 && set != 1))
+    return 0;
+  const ps::CommLayout lay = ps::comm_layout(world, max_tokens, hidden, es);
+  return static_cast<size_t>(lay.xg + static_cast<long long>(set) * max_tokens * hidden * es);
 }
 
 }  // extern "C"

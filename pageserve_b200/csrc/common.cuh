@@ -10,6 +10,7 @@
 #include "../../include/pageserve_b200.h"
 
 #define PS_DEVICE __device__ __forceinline__
+#define PS_HOST_DEVICE __host__ __device__ __forceinline__
 
 namespace ps {
 

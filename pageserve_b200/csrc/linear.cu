@@ -114,9 +114,9 @@ int ps_w8a16_linear_tiled(void* y, const void* x, const int8_t* q_tiled, const f
 
 size_t ps_w8a16_linear_tiled_workspace_size(int M, int N, int K) { return ps_host::linear_tc_workspace(M, N, K); }
 
-int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale, int M, int N,
-                   int K, int dtype, void* const* rank_bufs, int world, int rank, int set, int max_tokens, void* ws,
-                   size_t ws_bytes, ps_stream_t stream) {
+static int linear_push_any(const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale,
+                           int M, int N, int K, int dtype, void* const* rank_bufs, int world, int rank, int set,
+                           int max_tokens, void* ws, size_t ws_bytes, ps_stream_t stream, bool scatter) {
   const bool int8 = wdtype == PS_I8;
   if (M <= 0 || N <= 0 || K <= 0 || M > max_tokens || !x || (int8 ? (!w_tiled || !scale) : !w)) {
     ps_host::set_error("linear_push: invalid arguments (M=%d N=%d K=%d max_tokens=%d)", M, N, K, max_tokens);
@@ -132,7 +132,7 @@ int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_til
     return PS_ERR_INVALID;
   }
   ps::PushTargets pt;
-  const int rc = ps_host::push_targets(&pt, rank_bufs, world, rank, set, max_tokens, N, 2);
+  const int rc = ps_host::push_targets(&pt, rank_bufs, world, rank, set, max_tokens, N, 2, scatter);
   if (rc != PS_OK) return rc;
   const int8_t* wt = int8 ? w_tiled : nullptr;
   if (int8 && M <= ps_host::mma_max_m()) {
@@ -145,6 +145,20 @@ int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_til
                                     wt, &pt);
   if (r2 == PS_ERR_UNSUPPORTED) ps_host::set_error("linear_push: no tensor-core configuration for this shape");
   return r2;
+}
+
+int ps_linear_push(const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale, int M, int N,
+                   int K, int dtype, void* const* rank_bufs, int world, int rank, int set, int max_tokens, void* ws,
+                   size_t ws_bytes, ps_stream_t stream) {
+  return linear_push_any(x, w, wdtype, w_tiled, scale, M, N, K, dtype, rank_bufs, world, rank, set, max_tokens, ws,
+                         ws_bytes, stream, false);
+}
+
+int ps_linear_push_scatter(const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale, int M,
+                           int N, int K, int dtype, void* const* rank_bufs, int world, int rank, int set,
+                           int max_tokens, void* ws, size_t ws_bytes, ps_stream_t stream) {
+  return linear_push_any(x, w, wdtype, w_tiled, scale, M, N, K, dtype, rank_bufs, world, rank, set, max_tokens, ws,
+                         ws_bytes, stream, true);
 }
 
 int ps_linear_swiglu(void* y, const void* x, const void* w, int wdtype, const int8_t* w_tiled, const float* scale,

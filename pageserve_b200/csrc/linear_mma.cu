@@ -151,7 +151,12 @@ __global__ void __launch_bounds__(W * 32) linear_mma_kernel(
         const long long o = static_cast<long long>(m) * N + n;
         if (resid) v = to_f32(from_f32<T>(v)) + to_f32(resid[o]);
         if (push.world > 0) {
-          for (int d = 0; d < push.world; ++d) static_cast<T*>(push.dst[d])[o] = from_f32<T>(v);  // every rank's slot
+          if (push.slice) {  // two-shot: the owner of column n only
+            const int d = n / push.slice;
+            static_cast<T*>(push.dst[d])[push_offset(push, m, n, N, d)] = from_f32<T>(v);
+          } else {
+            for (int d = 0; d < push.world; ++d) static_cast<T*>(push.dst[d])[o] = from_f32<T>(v);  // every rank's slot
+          }
         } else {
           y[o] = from_f32<T>(v);
         }

@@ -430,7 +430,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (p.swiglu) {
                 tma_store_2d(&om.y, out_sa + sub * BM * 128, (n0 + sub * 128) / 2, m0);
               } else if (p.push.world > 0) {
-                for (int d = 0; d < p.push.world; ++d) tma_store_2d(&om.dst[d], out_sa + sub * BM * 256, n0 + sub * 128, m0);
+                const int n = n0 + sub * 128;
+                if (p.push.slice) {  // two-shot: the owner of these 128 columns only
+                  const int d = n / p.push.slice;
+                  if (n < p.N) tma_store_2d(&om.dst[d], out_sa + sub * BM * 256, n - d * p.push.slice, m0);
+                } else {
+                  for (int d = 0; d < p.push.world; ++d) tma_store_2d(&om.dst[d], out_sa + sub * BM * 256, n, m0);
+                }
               } else {
                 tma_store_2d(&om.y, out_sa + sub * BM * 256, n0 + sub * 128, m0);
               }
@@ -520,8 +526,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (resid) acc[j] = to_f32(from_f32<T>(acc[j])) + rv[j];
               }
               const uint4 pk = pack8<T>(acc);
-              for (int d = 0; d < ndst; ++d)  // push: every rank's slot (peers over NVLink)
-                *reinterpret_cast<uint4*>((p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off) = pk;
+              if (p.push.world > 0 && p.push.slice) {  // two-shot: the owner of these columns only
+                const int d = gn / p.push.slice;
+                *reinterpret_cast<uint4*>(static_cast<T*>(p.push.dst[d]) + push_offset(p.push, gm, gn, p.N, d)) = pk;
+              } else {
+                for (int d = 0; d < ndst; ++d)  // push: every rank's slot (peers over NVLink)
+                  *reinterpret_cast<uint4*>((p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off) = pk;
+              }
             } else {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -853,8 +864,9 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
     if (swiglu) {
       ok = ok && make_map(&om.y, y, xdt, 2, M, N / 2, 64, pl.bm, CU_TENSOR_MAP_SWIZZLE_NONE);
     } else if (push) {
+      const int cols = push->slice ? push->slice : N;  // two-shot slots hold one column slice
       for (int d = 0; d < push->world; ++d)
-        ok = ok && make_map(&om.dst[d], push->dst[d], xdt, 2, push->max_tokens, N, 128, pl.bm,
+        ok = ok && make_map(&om.dst[d], push->dst[d], xdt, 2, push->max_tokens, cols, 128, pl.bm,
                             CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
       ok = ok && make_map(&om.y, y, xdt, 2, M, N, 128, pl.bm, CU_TENSOR_MAP_SWIZZLE_NONE);

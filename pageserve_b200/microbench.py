@@ -207,6 +207,17 @@ def bench_tp_reduce(M=576, H=2048, K_full=2048, iters=20, warmup=3, seed=0):
         comm.linear_push(x, w, s_, workspace=ws)
         comm.allreduce_rmsnorm(xr, nw, 1e-6, s_)
 
+    two_shot = H % world == 0 and (H // world) % 128 == 0 and world > 1
+    it2 = [0]
+    x_old = [xr]
+
+    def fused2():  # two-shot: scatter, reduce + all-gather, local norm; sets alternate
+        s_ = it2[0] & 1
+        it2[0] += 1
+        comm.linear_push(x, w, s_, workspace=ws, scatter=True)
+        comm.reduce_norm(x_old[0], nw, 1e-6, s_, M)
+        x_old[0] = comm.gathered_ptr(s_)
+
     def local():
         y = w.linear(x, residual=xr, workspace=ws)
         rms_norm_fused(y, nw, 1e-6)
@@ -221,8 +232,10 @@ def bench_tp_reduce(M=576, H=2048, K_full=2048, iters=20, warmup=3, seed=0):
         dist.all_reduce(xr)
 
     out = {"case": "tp_reduce", "world": world, "M": M, "H": H, "K_shard": K}
-    for name, fn in (("nccl_us", nccl), ("fused_us", fused), ("local_us", local), ("push_only_us", push_only),
-                     ("linear_only_us", linear_only), ("nccl_allreduce_only_us", allreduce_only)):
+    cases = [("nccl_us", nccl), ("fused_us", fused)] + ([("fused2_us", fused2)] if two_shot else []) + \
+        [("local_us", local), ("push_only_us", push_only), ("linear_only_us", linear_only),
+         ("nccl_allreduce_only_us", allreduce_only)]
+    for name, fn in cases:
         dist.barrier()
         ms = _time(fn, iters, warmup)
         t = torch.tensor([ms], device=dev)
@@ -263,8 +276,9 @@ def main(argv=None):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-        for m, kf in ((576, 2048), (576, 11008), (64, 2048), (64, 11008)):
-            r = bench_tp_reduce(M=m, K_full=kf, iters=a.iters, warmup=a.warmup)
+        for m, kf, h in ((576, 2048, 2048), (576, 11008, 2048), (64, 2048, 2048), (64, 11008, 2048),
+                         (128, 5120, 5120), (128, 27648, 5120)):
+            r = bench_tp_reduce(M=m, H=h, K_full=kf, iters=a.iters, warmup=a.warmup)
             if dist.get_rank() == 0:
                 print(json.dumps(r), flush=True)
         from . import _lib

@@ -164,6 +164,23 @@ def _one_copy(lw: "LayerWeights", fl: "FusedLayer", dtype) -> None:
         lw.up_w = RowView(fl.gate_up, slice(1, None, 2), dtype)
 
 
+def two_shot_ok(world: int, hidden: int) -> bool:
+    """The two-shot reduction scatters whole 128-column output tiles."""
+    return world > 1 and hidden % world == 0 and (hidden // world) % 128 == 0
+
+
+def auto_tp_comm(world: int, hidden: int) -> str:
+    """Row-parallel reduction transport for ``tp_comm="auto"``: the one-shot
+    push at 2 ranks (one peer, one exchange), the two-shot push above that
+    when the hidden size splits into 128-column slices (each rank moves
+    2 (W-1)/W of its output instead of W-1 copies), else NCCL."""
+    if world <= 2:
+        return "fused"
+    if two_shot_ok(world, hidden):
+        return "fused2"
+    return "fused" if world <= 4 else "nccl"
+
+
 def _check_device_dtype(device, dtype) -> None:
     if torch.device(device).type != "cuda":
         raise RuntimeError("pageserve_b200.PagedCausalLM runs on CUDA only (no CPU fallback); pass device='cuda'")
@@ -213,12 +230,12 @@ class PagedCausalLM:
         ``synthetic.Qwen2Shape`` (the seeded random-init checkpoints). With
         ``tp`` (a ``tensor_parallel.TPGroup``) this rank loads only its
         Megatron shard (engine/tensor_parallel.py). ``tp_comm`` picks the
-        row-parallel reduction: "fused" (peer-memory push from the linear into
-        the next RMSNorm, at most ``tp_max_tokens`` tokens per step), "nccl"
-        (torch.distributed all_reduce, the reference's collective) or "auto"
-        (fused up to 4 ranks, where it measured faster than NCCL; NCCL at 8,
-        where every rank pushing its whole output to 7 peers moves several
-        times the data of a reduce-scatter + all-gather)."""
+        row-parallel reduction: "fused" (one-shot peer-memory push from the
+        linear into the next RMSNorm, at most ``tp_max_tokens`` tokens per
+        step), "fused2" (two-shot: the linear scatters column slices to their
+        owner ranks, which reduce, all-gather the residual stream and
+        normalise), "nccl" (torch.distributed all_reduce, the reference's
+        collective) or "auto" (``auto_tp_comm``)."""
         cfg = SimpleNamespace(num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
                               hidden_size=shape.hidden, head_dim=shape.head_dim, rms_norm_eps=shape.rms_eps,
                               rope_theta=shape.rope_theta, rope_parameters=None,
@@ -368,13 +385,16 @@ class PagedCausalLM:
         self._attn_side = torch.cuda.Stream(device=self.device)
         self._attn_concurrent = os.environ.get("PS_ATTN_CONCURRENT", "1") != "0"
         self.lin_ws = LinearWorkspace()
-        if tp_comm not in ("fused", "nccl", "auto"):
-            raise ValueError(f"tp_comm must be 'fused', 'nccl' or 'auto', not {tp_comm!r}")
+        if tp_comm not in ("fused", "fused2", "nccl", "auto"):
+            raise ValueError(f"tp_comm must be 'fused', 'fused2', 'nccl' or 'auto', not {tp_comm!r}")
         if tp_comm == "auto":
-            tp_comm = "fused" if (self.tp is not None and self.tp.world <= 4) else "nccl"
+            tp_comm = auto_tp_comm(self.tp.world if self.tp is not None else 1, self.hidden_size)
+        if tp_comm == "fused2" and self.tp is not None and not two_shot_ok(self.tp.world, self.hidden_size):
+            raise ValueError(f"tp_comm='fused2' needs hidden/world a multiple of 128 "
+                             f"(hidden {self.hidden_size}, world {self.tp.world})")
         self.tp_comm = tp_comm if self.tp is not None else None
         self.comm = None
-        if self.tp is not None and tp_comm == "fused":
+        if self.tp is not None and tp_comm in ("fused", "fused2"):
             from .comm import FusedAllReduce
             self.comm = FusedAllReduce.create(self.tp.rank, self.tp.world, tp_max_tokens, self.hidden_size, dtype,
                                               self.device, self.tp.group)
@@ -431,6 +451,8 @@ class PagedCausalLM:
         comm = self.comm  # fused TP reduction: o_proj -> set 0, down_proj -> set 1, consumed by the next norm
         if comm is not None and T > comm.max_tokens:
             raise ValueError(f"{T} tokens exceed tp_max_tokens={comm.max_tokens}")
+        if comm is not None and self.tp_comm == "fused2":
+            return self._forward_two_shot(x, q, attn, positions, slots, meta, runs, logits_rows)
         pending = False  # a down_proj reduction waits in set 1
         for li, fl in enumerate(self.fused):
             if pending:
@@ -469,6 +491,43 @@ class PagedCausalLM:
                 x = x.index_select(0, logits_rows)
             x = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
         return linear16(x, self.lm_head_w, workspace=self.lin_ws)
+
+    def _forward_two_shot(self, x, q, attn, positions, slots, meta, runs, logits_rows):
+        """The layer loop with the two-shot fused reduction: each row-parallel
+        linear scatters its output's column slices to their owner ranks, whose
+        reduce kernel adds the residual, all-gathers the new residual stream
+        (kept in the receive buffer's gathered region) and normalises it for
+        the next linear (engine/model.py:164-193 with the all-reduce of
+        engine/tensor_parallel.py:47)."""
+        T = x.shape[0]
+        hq, hkv, d = self.heads_local, self.kv_heads_local, self.head_dim
+        lib = _lib.load()
+        stream = _lib.stream_ptr(self.device)
+        comm = self.comm
+        num_slots = self.num_blocks * self.block_size
+        resid = x  # the residual stream: the embedding, then the gathered region of the last set reduced
+        h = rms_norm_fused(x, self.fused[0].input_ln, self.rms_eps) if self.fused else None
+        for li, fl in enumerate(self.fused):
+            qkv = self._linear(h, fl.qkv, fl.qkv_b)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            _lib.check(lib.ps_rope_qkv_write_kv(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), qkv.data_ptr(),
+                                                positions.data_ptr(), slots.data_ptr(), self.rope_cos.data_ptr(),
+                                                self.rope_sin.data_ptr(), self.max_position_embeddings, T, hq, hkv,
+                                                d, num_slots, _lib.dtype_code(self.dtype), stream), "rope_qkv")
+            self._attention(q, kc, vc, meta, runs, attn)
+            comm.linear_push(attn.view(T, hq * d), fl.o, 0, workspace=self.lin_ws, scatter=True)
+            h = comm.reduce_norm(resid, fl.post_ln, self.rms_eps, 0, T)
+            resid = comm.gathered_ptr(0)
+            act = linear_swiglu(h, fl.gate_up)
+            comm.linear_push(act, fl.down, 1, workspace=self.lin_ws, scatter=True)
+            nxt = self.fused[li + 1].input_ln if li + 1 < len(self.fused) else self.final_norm_w
+            h = comm.reduce_norm(resid, nxt, self.rms_eps, 1, T)
+            resid = comm.gathered_ptr(1)
+        if h is None:
+            h = rms_norm_fused(x, self.final_norm_w, self.rms_eps)
+        if logits_rows is not None:
+            h = h.index_select(0, logits_rows)
+        return linear16(h, self.lm_head_w, workspace=self.lin_ws)
 
     def _attention(self, q, kc, vc, meta, runs, attn) -> None:
         """Paged attention of every run into its rows of ``attn``; with both

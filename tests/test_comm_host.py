@@ -19,9 +19,14 @@ def test_buffer_bytes_layout():
     if not _lib.LIB_PATH.exists():
         pytest.skip("library not built")
     lib = _lib.load()
-    # control words + [2 sets][world][max_tokens][hidden] of 2-byte elements
-    assert lib.ps_comm_buffer_bytes(2, 576, 2048, _lib.PS_BF16) == 1024 + 2 * 2 * 576 * 2048 * 2
-    assert lib.ps_comm_buffer_bytes(8, 1, 8, _lib.PS_F16) == 1024 + 2 * 8 * 8 * 2
+    # control words (4 KB) + the gathered residual [2 sets][max_tokens][hidden] (256-byte padded)
+    # + slots [2 sets][world][max_tokens][hidden] of 2-byte elements
+    assert lib.ps_comm_buffer_bytes(2, 576, 2048, _lib.PS_BF16) == 4096 + 2 * 576 * 2048 * 2 + 2 * 2 * 576 * 2048 * 2
+    assert lib.ps_comm_buffer_bytes(8, 1, 8, _lib.PS_F16) == 4096 + 256 + 2 * 8 * 8 * 2
+    # the gathered region of set s starts after the control words
+    assert lib.ps_comm_gathered_offset(2, 576, 2048, _lib.PS_BF16, 0) == 4096
+    assert lib.ps_comm_gathered_offset(2, 576, 2048, _lib.PS_BF16, 1) == 4096 + 576 * 2048 * 2
+    assert lib.ps_comm_gathered_offset(2, 576, 2048, _lib.PS_BF16, 2) == 0
     assert lib.ps_comm_buffer_bytes(9, 1, 8, _lib.PS_BF16) == 0  # above PS_COMM_MAX_WORLD
     assert lib.ps_comm_buffer_bytes(2, 1, 8, _lib.PS_F32) == 0   # 16-bit activations only
     assert lib.ps_comm_buffer_bytes(0, 1, 8, _lib.PS_BF16) == 0
@@ -92,3 +97,15 @@ def test_handle_exchange_two_ranks():
                 assert res[r]["bufs"][p] == 0x7000000 + 0x10000 * (p + 1)  # opened from rank p's handle
         assert res[r]["freed"] == [own]
         assert sorted(res[r]["closed"]) == sorted(b for i, b in enumerate(res[r]["bufs"]) if i != r)
+
+
+def test_auto_tp_transport_choice():
+    """tp_comm="auto": one-shot push at 2 ranks, two-shot where the hidden
+    size splits into 128-column slices, else the one-shot push up to 4 ranks
+    and NCCL beyond."""
+    from pageserve_b200.model import auto_tp_comm, two_shot_ok
+    assert auto_tp_comm(2, 2048) == "fused"
+    assert auto_tp_comm(4, 2048) == "fused2" and auto_tp_comm(8, 2048) == "fused2"   # 3B: 512 / 256 columns
+    assert auto_tp_comm(8, 5120) == "fused2" and auto_tp_comm(4, 5120) == "fused2"   # 32B: 640 / 1280 columns
+    assert auto_tp_comm(4, 896) == "fused" and auto_tp_comm(8, 896) == "nccl"        # 0.5B: 224 / 112 columns
+    assert two_shot_ok(2, 256) and not two_shot_ok(1, 2048) and not two_shot_ok(3, 2048)

@@ -95,6 +95,68 @@ def test_push_then_allreduce_rmsnorm(world, M, N, K, int8):
         ranks[0].close()
 
 
+@pytest.mark.parametrize("world,M,N,K,int8", [
+    (2, 576, 2048, 1024, True),    # TP2 o_proj of the 3B shape (split-K writer)
+    (4, 576, 2048, 512, True),     # TP4 o_proj, prefill+decode batch
+    (8, 576, 2048, 256, True),     # TP8 o_proj: 256-column slices
+    (8, 9, 2048, 1376, True),      # TP8 down_proj at decode size (mma.sync small-M writer)
+    (4, 128, 5120, 1280, True),    # 32B shape TP4 o_proj, config-5 batch
+    (2, 40, 512, 640, False),      # 16-bit weight
+])
+def test_two_shot_scatter_reduce_gather_rmsnorm(world, M, N, K, int8):
+    """Two-shot form: ps_linear_push_scatter sends each column slice to its
+    owner rank, ps_tp_reduce_rmsnorm (phase 1 on every rank, then phase 2 on
+    every rank: no kernel waits on a later launch) reduces the slice, adds the
+    residual, all-gathers it and normalises. The gathered residual stream is
+    bit-exact (the same partials and rank order as the unfused sum), identical
+    on every rank, and feeds the next set's reduction as its x_old; rounds
+    alternate the sets, so the flags and row-block counters re-arm."""
+    _need_gpu()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(world * 77 + M)
+    ranks = FusedAllReduce.emulated(world, max_tokens=max(M, 64), hidden=N, dtype=torch.bfloat16, device=dev)
+    try:
+        xs = [torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16) for _ in range(world)]
+        ws = _weights(world, N, K, int8, dev, g)
+        norm_w = (1 + 0.1 * torch.randn(N, device=dev, generator=g)).to(torch.bfloat16)
+        resid = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+        partials = [_partial(xs[r], ws[r]) for r in range(world)]
+        s = torch.zeros(M, N, dtype=torch.float32, device=dev)
+        for p in partials:
+            s += p.float()
+        s = s.to(torch.bfloat16)
+        x_exp = resid
+        x_old = [resid] * world
+        for it in range(3):
+            for set_ in (0, 1):
+                for r in range(world):
+                    ranks[r].linear_push(xs[r], ws[r], set_, scatter=True)
+                for r in range(world):
+                    ranks[r].reduce_norm(x_old[r], norm_w, 1e-6, set_, M, phases=1)
+                ys = [ranks[r].reduce_norm(x_old[r], norm_w, 1e-6, set_, M, phases=2) for r in range(world)]
+                torch.cuda.synchronize()
+                x_exp = (x_exp.float() + s.float()).to(torch.bfloat16)
+                y_ref = rms_norm_fused(x_exp, norm_w, 1e-6)
+                for r in range(world):
+                    assert torch.equal(ranks[r].gathered(set_, M), x_exp), f"round {it} set {set_} rank {r}: residual"
+                    assert torch.equal(ys[r], ys[0]), f"round {it} set {set_}: ranks disagree"
+                assert rel_err(ys[0].float(), y_ref.float()) < REL_TOL
+                x_old = [ranks[r].gathered_ptr(set_) for r in range(world)]
+        # the plain all-reduce (no residual, no norm): y = T(sum of partials)
+        for r in range(world):
+            ranks[r].linear_push(xs[r], ws[r], 0, scatter=True)
+        for r in range(world):
+            ranks[r].reduce_norm(None, None, 0.0, 0, M, phases=1)
+        outs = [ranks[r].reduce_norm(None, None, 0.0, 0, M, phases=2) for r in range(world)]
+        torch.cuda.synchronize()
+        for r in range(world):
+            assert torch.equal(outs[r], s), f"rank {r}: plain two-shot all-reduce"
+        _lib.raise_on_device_error()
+    finally:
+        ranks[0].close()
+
+
 def test_row_parallel_linear_on_push_transport_matches_oracle():
     """tensor_parallel.py:34-48 semantics (the sum of the ranks' partials of
     a column-split weight) against the numpy oracle."""

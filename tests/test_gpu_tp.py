@@ -58,7 +58,7 @@ def _tp_worker(rank, world, port, out_file, tp_comm):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tp_comm,port", [("fused", 29517), ("nccl", 29519)])
+@pytest.mark.parametrize("tp_comm,port", [("fused", 29517), ("fused2", 29518), ("nccl", 29519)])
 def test_tp2_matches_tp1(tp_comm, port):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
