@@ -78,6 +78,17 @@ PS_API int ps_write_kv(void* k_cache_dev, void* v_cache_dev, const int32_t* bloc
                 int num_blocks, int block_size, int num_kv_heads, int head_dim, int dtype, int start_pos,
                 int num_tokens, const void* k_dev, const void* v_dev, ps_stream_t stream);
 
+/* Copy-on-write of KV blocks for prefix sharing (engine/prefix_cache.py:35-82
+ * shares physical blocks between sequences; a sequence that continues from a
+ * shared, partially filled block writes into a private copy instead). For each
+ * of the n_pairs (src, dst) int32 pairs in pairs_dev, block dst of every layer
+ * of both caches ([num_layers][num_blocks][block_size][num_kv_heads][head_dim],
+ * the layout of engine/model.py:143-147) becomes a copy of block src. Ids
+ * outside [0, num_blocks) skip the pair and are recorded in the status word. */
+PS_API int ps_copy_kv_blocks(void* k_cache_dev, void* v_cache_dev, const int32_t* pairs_dev, int n_pairs,
+                             int num_layers, int num_blocks, int block_size, int num_kv_heads, int head_dim,
+                             int dtype, ps_stream_t stream);
+
 /* Batched form of the slot mapping used by write_kv (engine/paged_attention.py:74-77)
  * for a step of several sequences: for sequence b with chunk tokens
  * [cu_q[b], cu_q[b+1]) starting at position start_pos[b], writes

@@ -171,9 +171,70 @@ int elem_size(int dtype) {
   return 0;
 }
 
+// ------------------------------------------------------------- copy_blocks --
+// Copy-on-write of KV blocks: for every (src, dst) pair and every layer, the
+// whole block (block_size x Hkv x D) of K and V is copied. One CTA-stride loop
+// over (pair, layer, K/V, 16-byte unit). Ids outside [0, num_blocks) skip the
+// pair and are recorded.
+__global__ void copy_blocks_kernel(uint4* __restrict__ k_cache, uint4* __restrict__ v_cache,
+                                   const int32_t* __restrict__ pairs, int n_pairs, int num_layers,
+                                   long long layer_units, long long block_units, int num_blocks, int* status) {
+  const long long per_pair = 2LL * num_layers * block_units;
+  const long long work = per_pair * n_pairs;
+  for (long long w = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; w < work;
+       w += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(w / per_pair);
+    long long r = w - static_cast<long long>(p) * per_pair;
+    const int which = static_cast<int>(r / (num_layers * block_units));  // 0 = K, 1 = V
+    r -= static_cast<long long>(which) * num_layers * block_units;
+    const int layer = static_cast<int>(r / block_units);
+    const long long u = r - static_cast<long long>(layer) * block_units;
+    const int src = pairs[2 * p], dst = pairs[2 * p + 1];
+    if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
+      record_error(status, kErrBlockId);
+      continue;
+    }
+    uint4* c = which ? v_cache : k_cache;
+    const long long base = static_cast<long long>(layer) * layer_units;
+    c[base + static_cast<long long>(dst) * block_units + u] = c[base + static_cast<long long>(src) * block_units + u];
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+int ps_copy_kv_blocks(void* k_cache, void* v_cache, const int32_t* pairs, int n_pairs, int num_layers, int num_blocks,
+                      int block_size, int num_kv_heads, int head_dim, int dtype, ps_stream_t stream) {
+  const int es = elem_size(dtype);
+  if (!es || dtype == PS_I8) {
+    ps_host::set_error("copy_kv_blocks: unsupported dtype %d", dtype);
+    return PS_ERR_UNSUPPORTED;
+  }
+  if (n_pairs < 0 || num_layers <= 0 || num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0 || head_dim <= 0) {
+    ps_host::set_error("copy_kv_blocks: invalid sizes");
+    return PS_ERR_INVALID;
+  }
+  if (n_pairs == 0) return PS_OK;
+  if (!k_cache || !v_cache || !pairs) {
+    ps_host::set_error("copy_kv_blocks: null pointer");
+    return PS_ERR_INVALID;
+  }
+  const long long block_bytes = static_cast<long long>(block_size) * num_kv_heads * head_dim * es;
+  if (block_bytes % 16 != 0 || !ps_host::aligned(k_cache, 16) || !ps_host::aligned(v_cache, 16)) {
+    ps_host::set_error("copy_kv_blocks: blocks must be whole 16-byte units and the caches 16-byte aligned");
+    return PS_ERR_INVALID;
+  }
+  const long long block_units = block_bytes / 16;
+  const long long layer_units = block_units * num_blocks;
+  const int threads = 256;
+  copy_blocks_kernel<<<grid_for(2LL * n_pairs * num_layers * block_units, threads), threads, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), pairs, n_pairs, num_layers, layer_units,
+      block_units, num_blocks, ps_host::status_word(PS_TU_KV));
+  ps_host::count_launch();
+  return ps_host::check_launch("copy_kv_blocks");
+}
 
 int ps_write_kv(void* k_cache, void* v_cache, const int32_t* table, int table_len, int num_blocks,
                 int block_size, int num_kv_heads, int head_dim, int dtype, int start_pos, int num_tokens,

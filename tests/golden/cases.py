@@ -122,3 +122,20 @@ def greedy_inputs(name: str):
         at += n
     assert at <= GREEDY_POOL
     return prompts, tables
+
+
+# Continuous-batching trace (make_golden.make_sched_trace): an 8-block pool of
+# 4-token blocks, 3 sequences per step and 8 tokens per step over 5 requests,
+# so prefill is chunked and the pool runs out (preemption + recompute).
+SCHED_TRACE = {"num_blocks": 8, "block_size": 4, "max_batch_size": 3, "token_budget": 8,
+               "prompt_lens": (5, 11, 3, 17, 8), "max_new": (6, 3, 9, 4, 5), "vocab": 512}
+
+
+def sched_trace_prompts():
+    rng = np.random.default_rng(404)
+    return [rng.integers(0, SCHED_TRACE["vocab"], size=n).astype(np.int64) for n in SCHED_TRACE["prompt_lens"]]
+
+
+def fake_next_token(input_ids, start_pos) -> int:
+    """A deterministic stand-in for the model's greedy token."""
+    return int((sum(int(t) for t in input_ids) * 31 + int(start_pos) * 7 + len(input_ids)) % SCHED_TRACE["vocab"])

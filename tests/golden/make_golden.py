@@ -30,6 +30,9 @@ Fixtures:
   greedy_<name>.npz        greedy decode, 4 sequences x (prefill + 32 decode
                            steps), float32 and the reference's own bf16 picks
                            (cases.GREEDY_CASES)
+  sched_trace.npz          the reference's scheduler + runner over a small
+                           pool (chunked prefill, preemption) with a fake
+                           model: per step the snapshot, entries and calls
 """
 
 from __future__ import annotations
@@ -353,10 +356,69 @@ def make_greedy():
         np.savez_compressed(HERE / f"greedy_{name}.npz", **res)
 
 
+def make_sched_trace():
+    """The reference's own continuous batching (engine/scheduler.py +
+    engine/runner.py's ContinuousBatchingRunner, unmodified) over a small
+    block pool that forces chunked prefill, preemption and recompute, with a
+    deterministic fake model (cases.fake_next_token). Records, per scheduler
+    step, the running sequences' state the runner snapshots before step(), the
+    batch entries, and every process_chunk call with the token it returned."""
+    import threading
+
+    from engine.block_allocator import BlockAllocator
+    from engine.runner import ContinuousBatchingRunner
+    from engine.scheduler import Scheduler
+    from engine.sequence import Sequence
+
+    steps = []
+    calls = []
+    lock = threading.Lock()
+
+    class RecordingScheduler(Scheduler):
+        def step(self):
+            snap = [(s.seq_id, s.num_prompt_tokens_processed, len(s.output_tokens)) for s in self.running]
+            batch = super().step()
+            steps.append({"snapshot": snap, "entries": [(e.seq.seq_id, e.chunk, e.produces_token) for e in batch]})
+            return batch
+
+    def process_chunk(input_ids, block_table, start_pos):
+        tok = cases.fake_next_token(input_ids, start_pos)
+        with lock:
+            calls.append((list(input_ids), list(block_table), int(start_pos), tok, len(steps) - 1))
+        return tok
+
+    spec = cases.SCHED_TRACE
+    alloc = BlockAllocator(num_blocks=spec["num_blocks"], block_size=spec["block_size"])
+    sched = RecordingScheduler(alloc, block_size=spec["block_size"], max_batch_size=spec["max_batch_size"],
+                               token_budget=spec["token_budget"])
+    prompts = cases.sched_trace_prompts()
+    seqs = [Sequence(prompt_tokens=list(p), max_new_tokens=n) for p, n in zip(prompts, spec["max_new"])]
+    id_of = {s.seq_id: i for i, s in enumerate(seqs)}  # global seq ids -> request index
+    for s in seqs:  # every request present before the runner's thread starts: a deterministic trace
+        sched.add_request(s)
+    runner = ContinuousBatchingRunner(sched, process_chunk)
+    for s in seqs:
+        runner.wait_until_finished(s, timeout=60)
+    runner.stop()
+    out = {"n_steps": np.asarray(len(steps))}
+    for k, st in enumerate(steps):
+        out[f"{k}/snapshot"] = np.asarray([(id_of[a], b, c) for a, b, c in st["snapshot"]], np.int64).reshape(-1, 3)
+        out[f"{k}/entries"] = np.asarray([(id_of[a], b, int(c)) for a, b, c in st["entries"]], np.int64).reshape(-1, 3)
+    for j, (ids, table, start, tok, k) in enumerate(calls):
+        out[f"call{j}/ids"] = np.asarray(ids, np.int64)
+        out[f"call{j}/table"] = np.asarray(table, np.int64)
+        out[f"call{j}/meta"] = np.asarray([start, tok, k], np.int64)
+    out["n_calls"] = np.asarray(len(calls))
+    for i, s in enumerate(seqs):
+        out[f"out{i}"] = np.asarray(s.output_tokens, np.int64)
+    np.savez_compressed(HERE / "sched_trace.npz", **out)
+    print(f"  {len(steps)} scheduler steps, {len(calls)} process_chunk calls", flush=True)
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["attention", "quant", "norm_rope", "tp", "tiny", "cfg1", "greedy"]
+    which = sys.argv[1:] or ["attention", "quant", "norm_rope", "tp", "tiny", "cfg1", "greedy", "sched"]
     for w in which:
         print("generating", w, flush=True)
         {"attention": make_attention, "quant": make_quant, "norm_rope": make_norm_rope, "tp": make_tp,
-         "tiny": make_tiny_model, "cfg1": make_cfg1, "greedy": make_greedy}[w]()
+         "tiny": make_tiny_model, "cfg1": make_cfg1, "greedy": make_greedy, "sched": make_sched_trace}[w]()
     print("done")

@@ -100,12 +100,10 @@ def test_handle_exchange_two_ranks():
 
 
 def test_auto_tp_transport_choice():
-    """tp_comm="auto": one-shot push at 2 ranks, two-shot where the hidden
-    size splits into 128-column slices, else the one-shot push up to 4 ranks
-    and NCCL beyond."""
+    """tp_comm="auto": the one-shot push at 2 ranks, NCCL from 4 (measured);
+    the two-shot transport needs 128-column slices."""
     from pageserve_b200.model import auto_tp_comm, two_shot_ok
     assert auto_tp_comm(2, 2048) == "fused"
-    assert auto_tp_comm(4, 2048) == "fused2" and auto_tp_comm(8, 2048) == "fused2"   # 3B: 512 / 256 columns
-    assert auto_tp_comm(8, 5120) == "fused2" and auto_tp_comm(4, 5120) == "fused2"   # 32B: 640 / 1280 columns
-    assert auto_tp_comm(4, 896) == "fused" and auto_tp_comm(8, 896) == "nccl"        # 0.5B: 224 / 112 columns
-    assert two_shot_ok(2, 256) and not two_shot_ok(1, 2048) and not two_shot_ok(3, 2048)
+    assert auto_tp_comm(4, 2048) == "nccl" and auto_tp_comm(8, 5120) == "nccl"
+    assert two_shot_ok(8, 2048) and two_shot_ok(4, 5120) and two_shot_ok(2, 256)
+    assert not two_shot_ok(8, 896) and not two_shot_ok(1, 2048) and not two_shot_ok(3, 2048)
