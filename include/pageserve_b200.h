@@ -235,6 +235,24 @@ PS_API int ps_argmax(int32_t* out_dev, const void* logits_dev, int M, int V, int
 PS_API int ps_linear_swiglu(void* y_dev, const void* x_dev, const void* w_dev, int wdtype, const int8_t* w_tiled_dev,
                             const float* scale_dev, int M, int N2, int K, int dtype, ps_stream_t stream);
 
+/* ---------------------------------------- (f) on-device token selection
+ *
+ * The reference picks each sequence's next token on the host
+ * (int(logits[-1].argmax()), server.py:47-51, engine/runner.py:79-83);
+ * ps_argmax is the batched greedy form. These add top-k and sampling.
+ *
+ * Top-k of each of M rows (row stride ld elements, V columns, dtype PS_F32 /
+ * PS_BF16 / PS_F16): vals (float32, M x k) and idx (int32, M x k) sorted by
+ * value descending, ties by index ascending (so k = 1 equals ps_argmax).
+ * 1 <= k <= min(V, 1024). NaN ranks above +inf. */
+PS_API int ps_topk(float* vals_dev, int32_t* idx_dev, const void* logits_dev, int M, int V, int ld, int k, int dtype,
+                   ps_stream_t stream);
+/* Sampling from each row's top-k (ps_topk's outputs): p_j proportional to
+ * exp((v_j - v_0) / temperature), token = idx[first j whose cumulative p
+ * exceeds u * sum(p)], u = uniforms_dev[row] in [0, 1). temperature > 0. */
+PS_API int ps_sample_topk(int32_t* out_dev, const float* vals_dev, const int32_t* idx_dev, const float* uniforms_dev,
+                          int M, int k, float temperature, ps_stream_t stream);
+
 /* ------------------------------------- (e) fused tensor-parallel all-reduce
  *
  * Replaces the dist.all_reduce(partial, SUM) after each row-parallel linear

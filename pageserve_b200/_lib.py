@@ -68,6 +68,8 @@ _SIGNATURES = {
     "ps_tp_reduce_rmsnorm": (c_int, [_P, _P, _P, c_float, _I, _I, _I, _P, _I, _I, _I, _I, _I, _P]),
     "ps_comm_gathered_offset": (c_size_t, [_I, _I, _I, _I, _I]),
     "ps_copy_kv_blocks": (c_int, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "ps_topk": (c_int, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "ps_sample_topk": (c_int, [_P, _P, _P, _P, _I, _I, c_float, _P]),
 }
 
 _lock = threading.Lock()

@@ -573,20 +573,29 @@ class PagedCausalLM:
         return self.gather_logits(self._forward(ids, meta, None))
 
     def forward_batch(self, input_ids, q_lens: list[int], start_pos: list[int], block_tables: list[list[int]],
-                      return_logits: bool = True):
+                      return_logits: bool = True, top_k: int | None = None, temperature: float = 1.0,
+                      generator: torch.Generator | None = None):
         """One scheduler step for many sequences in one pass (superset of the
         reference, which calls forward_step once per sequence,
         engine/runner.py:65-79). input_ids: the chunks concatenated in
         sequence order. Returns (logits of each sequence's last token (B, V),
-        greedy next tokens int32 (B,))."""
+        next tokens int32 (B,)): greedy, or with ``top_k`` sampled on the
+        device from softmax(top-k logits / temperature)."""
         if self.k_cache is None:
             raise RuntimeError("allocate_kv_cache() must run before forward_batch()")
         ids = torch.as_tensor(input_ids, dtype=torch.int64).to(self.device).reshape(-1)
         meta = self.make_meta(q_lens, start_pos, block_tables)
         last = meta.cu_q[1:].to(torch.int64) - 1
         logits = self._forward(ids, meta, last)
-        nxt = self.next_tokens(logits)
-        return (self.gather_logits(logits) if return_logits else None), nxt
+        if top_k is None:
+            return (self.gather_logits(logits) if return_logits else None), self.next_tokens(logits)
+        from .sampling import sample_top_k
+        full = self.gather_logits(logits)
+        nxt = sample_top_k(full, top_k, temperature, generator=generator)
+        if self.tp is not None:  # every rank keeps rank 0's draw
+            import torch.distributed as dist
+            dist.broadcast(nxt, src=0, group=self.tp.group)
+        return (full if return_logits else None), nxt
 
     def gather_logits(self, logits: torch.Tensor) -> torch.Tensor:
         """Full-vocabulary logits (all-gathered over the vocab shards under TP)."""
