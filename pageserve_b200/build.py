@@ -76,7 +76,39 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+    build_torch_ops(force=force)
     return LIB
+
+
+TORCH_OPS_SRC = PKG / "torch_ops" / "pageserve_ops.cpp"
+TORCH_OPS_LIB = PKG / "libpageserve_torch_ops.so"
+
+
+def build_torch_ops(force: bool = False) -> Path:
+    """torch.ops.pageserve_b200.* (TORCH_LIBRARY registrations over the C
+    ABI): one g++ compile against torch's headers, linked to
+    libpageserve_b200.so (found next to it at run time) and torch's
+    libraries."""
+    import torch
+    import torch.utils.cpp_extension as ce
+
+    deps = [TORCH_OPS_SRC, ROOT / "include" / "pageserve_b200.h"]
+    if (not force and TORCH_OPS_LIB.exists() and
+            TORCH_OPS_LIB.stat().st_mtime >= max(d.stat().st_mtime for d in deps)):
+        return TORCH_OPS_LIB
+    incs = [f"-I{p}" for p in ce.include_paths(device_type="cuda")]
+    libdirs = ce.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = TORCH_OPS_LIB.with_suffix(".so.tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", *incs,
+           str(TORCH_OPS_SRC), "-o", str(tmp), f"-L{PKG}", "-lpageserve_b200", "-Wl,-rpath,$ORIGIN",
+           *[f"-L{d}" for d in libdirs], *[f"-Wl,-rpath,{d}" for d in libdirs],
+           "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch ops build failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TORCH_OPS_LIB)
+    return TORCH_OPS_LIB
 
 
 if __name__ == "__main__":
