@@ -70,12 +70,21 @@ constexpr int kSmemBudget = 216 * 1024;
 // only with -DPS_TRACE (never in the shipped library).
 #ifdef PS_TRACE
 __device__ unsigned long long g_tc_trace[4096];
+__device__ unsigned long long g_tc_trace2[4096];  // widen warp 3 lane 0, 8 points per k-tile
+#define PS_TC_TRACE2(i, k)                                                         \
+  do {                                                                             \
+    if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 256) \
+      g_tc_trace2[(i) * 8 + (k)] = clock64();                                      \
+  } while (0)
 #define PS_TC_TRACE(slot, cond)                                                    \
   do {                                                                             \
     if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)           \
       g_tc_trace[(slot)] = clock64();                                              \
   } while (0)
 #else
+#define PS_TC_TRACE2(i, k) \
+  do {                     \
+  } while (0)
 #define PS_TC_TRACE(slot, cond) \
   do {                          \
   } while (0)
@@ -98,6 +107,7 @@ struct TcParams {
   int splits;       // split-K CTAs per output tile = cluster size along z (1: no cluster)
   int tma_out;      // splits == 1 and N % 8 == 0: outputs leave by TMA stores (OutMaps)
   int swiglu;       // rows interleaved (2i gate_i, 2i+1 up_i): y[m][i] = silu(gate) * up, width N / 2
+  int stagger;      // rotate each CTA's k-tile order (see kt_of in the kernel)
   PushTargets push;  // world > 0: the final output goes to every rank's receive slot instead of y
 };
 
@@ -119,10 +129,17 @@ struct Cfg {
   static constexpr int kAccCols = NSUB * BM;                       // fp32 accumulators
   static constexpr int kACols = kInt8 ? NSUB * (kBK / 2) : 0;      // one TMEM A stage (2 bf16 per column)
   static constexpr int kStage = BM * 128 * 4;                     // epilogue fp32 stage [BM][128]
-  static constexpr int kRX0 = (96 * 1024) / kX;
+  static constexpr int kRX0 = (120 * 1024) / kX;
   static constexpr int kRX = kRX0 < 2 ? 2 : (kRX0 > 8 ? 8 : kRX0);
+  // Pre-tiled int8 weights arrive as one bulk copy of kJ consecutive k-tiles
+  // per 128-row block (contiguous in the tiled layout): a thread issues about
+  // one bulk copy per ~675 cycles whatever its size (measured on B200), so
+  // 8 KB copies would cap the weight stream below the MMA rate. The ring has
+  // kRW k-tile slots in groups of kJ, one full/empty barrier pair per group.
+  static constexpr int kJ = kInt8 ? 2 : 1;
   static constexpr int kRW0 = (kSmemBudget - kAS * kA - kRX * kX) / kW;
-  static constexpr int kRW = kRW0 < 2 ? 2 : (kRW0 > 8 ? 8 : kRW0);
+  static constexpr int kRW1 = kRW0 > 8 * kJ ? 8 * kJ : kRW0;
+  static constexpr int kRW = (kRW1 / kJ) * kJ < 2 * kJ ? 2 * kJ : (kRW1 / kJ) * kJ;
   // layout (1024-aligned rings first): A | W | X | barriers. The epilogue's
   // stage reuses the rings, idle once the main loop is done.
   static constexpr int kOffA = 0;
@@ -145,6 +162,7 @@ struct Cfg {
   static_assert(kRings >= NSUB * BM * 256, "TMA output tiles alias the rings");
   static_assert(kTmemNeed <= 512, "TMEM columns");
   static_assert(kW % 1024 == 0 && kX % 1024 == 0 && kA % 1024 == 0, "1024-byte aligned stages");
+  static_assert(kRW % kJ == 0 && kRW / kJ <= 8, "weight ring groups");
 };
 
 template <typename T, bool kInt8, int NSUB, int BM>
@@ -157,8 +175,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
-  auto a_addr = [&](int s) { return base + C::kOffA + s * C::kA; };
   auto w_addr = [&](int s) { return base + C::kOffW + s * C::kW; };
+  // Weight ring: WG groups of WJ k-tile slots; group g holds, per sub-tile,
+  // WJ consecutive 8 KB k-tile blocks (one bulk copy each for the tiled
+  // layout). Every ring index below divides by compile-time constants only:
+  // the per-k-tile loops are latency chains, and a runtime division costs
+  // more than the widening itself.
+  constexpr int WJ = C::kJ;
+  constexpr int WG = RW / WJ;
   auto x_addr = [&](int s) { return base + C::kOffX + s * C::kX; };
   const uint32_t bars = base + C::kOffBar;
   auto w_full = [&](int s) { return bars + 8 * s; };
@@ -183,12 +207,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kt0 = split * p.k_tiles_per_split;
   const int kt1 = min(p.k_tiles, kt0 + p.k_tiles_per_split);
   const int nkt = kt1 - kt0;
+  // K order: each CTA starts at a different whole weight group (rotation
+  // among the full groups of its split; a partial last group stays last), so
+  // the CTAs that share a token tile do not all request the same activation
+  // k-tile at once. Sequence position i -> k-tile offset inside the split.
+  const int nfull = nkt / WJ;
+  const int rot = (p.stagger && nfull > 1) ? static_cast<int>((blockIdx.x * 5u + blockIdx.y * 3u) % nfull) : 0;
+  auto kt_of = [&](int i) {
+    if (i >= nfull * WJ) return i;
+    const int g = i / WJ;
+    int ag = g + rot;
+    if (ag >= nfull) ag -= nfull;
+    return ag * WJ + (i - g * WJ);
+  };
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int s = 0; s < RW; ++s) {
+    for (int s = 0; s < WG; ++s) {
       mbar_init(w_full(s), 1);
-      mbar_init(w_empty(s), kInt8 ? kDeqWarps : 1);
+      mbar_init(w_empty(s), kInt8 ? kDeqWarps * WJ : 1);
     }
     for (int s = 0; s < RX; ++s) {
       mbar_init(x_full(s), 1);
@@ -222,23 +259,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------- weight producer --
-    for (int i = 0; i < nkt; ++i) {
-      const int s = i % RW;
-      if (i >= RW && !warp_wait(w_empty(s), ((i / RW) - 1) & 1, abort_flag, p.status)) break;
+    const int b0 = blockIdx.x * NSUB;
+    const int nb = min(NSUB, p.n_blocks - b0);  // row blocks past the last are not loaded (outputs masked)
+    for (int i = 0; i < nkt; i += WJ) {
+      const int grp = i / WJ;
+      const int s = grp % WG;
+      if (grp >= WG && !warp_wait(w_empty(s), ((grp / WG) - 1) & 1, abort_flag, p.status)) break;
       PS_TC_TRACE(16 + (i & 255) * 8 + 0, lane == 0);
       if (lane == 0) {
-        if (kInt8 && p.wt) {
-          // NSUB contiguous 8 KB blocks; blocks past the last row block are
-          // not loaded (their rows only feed outputs the epilogue masks).
-          const int b0 = blockIdx.x * NSUB;
-          const int nb = min(NSUB, p.n_blocks - b0);
-          mbar_expect_tx(w_full(s), nb * 8192);
-          for (int sub = 0; sub < nb; ++sub)
-            bulk_load(w_addr(s) + sub * 8192,
-                      p.wt + (static_cast<long long>(b0 + sub) * p.k_tiles + (kt0 + i)) * 8192, 8192, w_full(s));
+        const int kt = kt0 + kt_of(i);
+        const uint32_t dst = w_addr(s * WJ);
+        if (kInt8) {
+          const int nk = min(WJ, nkt - i);
+          mbar_expect_tx(w_full(s), nb * nk * 8192);
+          for (int sub = 0; sub < nb; ++sub) {
+            if (p.wt) {  // tiled: nk consecutive 8 KB k-tile blocks of row block b0+sub are contiguous
+              bulk_load(dst + sub * WJ * 8192, p.wt + (static_cast<long long>(b0 + sub) * p.k_tiles + kt) * 8192,
+                        nk * 8192, w_full(s));
+            } else {  // row-major: one 128-row x 64 box per k-tile
+              for (int j = 0; j < nk; ++j)
+                tma_load_2d(dst + (sub * WJ + j) * 8192, &wmap, w_full(s), (kt + j) * kBK, n0 + sub * 128);
+            }
+          }
         } else {
           mbar_expect_tx(w_full(s), C::kW);
-          tma_load_2d(w_addr(s), &wmap, w_full(s), (kt0 + i) * kBK, n0);
+          tma_load_2d(dst, &wmap, w_full(s), kt * kBK, n0);
         }
       }
       __syncwarp();
@@ -251,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       PS_TC_TRACE(16 + (i & 255) * 8 + 1, lane == 0);
       if (lane == 0) {
         mbar_expect_tx(x_full(s), C::kX);
-        tma_load_2d(x_addr(s), &xmap, x_full(s), (kt0 + i) * kBK, m0);
+        tma_load_2d(x_addr(s), &xmap, x_full(s), (kt0 + kt_of(i)) * kBK, m0);
       }
       __syncwarp();
     }
@@ -264,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int sa = kInt8 ? (i % AS) : (i % RW);
       ok = warp_wait(kInt8 ? a_full(sa) : w_full(sa), kInt8 ? ((i / AS) & 1) : ((i / RW) & 1), abort_flag,
                      p.status);
+      PS_TC_TRACE(16 + (i & 255) * 8 + 6, lane == 0);
       if (ok) ok = warp_wait(x_full(sx), (i / RX) & 1, abort_flag, p.status);
       if (!ok) break;
       tc_fence_after();
@@ -292,6 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     const int t = threadIdx.x - 96;  // 0 .. 32*kDeqWarps-1
+    (void)t;
     // ------------------------------------- int8 -> bf16 widening into TMEM --
     // Warp (q = warp % 4, h = (warp - 3) / 4) owns TMEM lanes [32q, 32q+32):
     // NSUB = 2: sub-tile h, the row's whole K tile (64 values, 32 columns);
@@ -306,35 +353,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int kChunks = NSUB == 2 ? 4 : 2;             // 16-byte chunks this lane widens
       const int c0 = NSUB == 2 ? 0 : 2 * h;
       const uint32_t tcol0 = (NSUB == 2 ? sub * (kBK / 2) : h * (kBK / 4));
+      const unsigned char* wring = gbase + C::kOffW + (sub * WJ) * 8192 + rin * 64;
+      const uint32_t tlane = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::kAccCols + tcol0;
       for (int i = 0; i < nkt; ++i) {
-        const int sw = i % RW;
+        const int grp = i / WJ;
+        const int jj = i - grp * WJ;
+        const int sw = grp % WG;
         const int sa = i % AS;
-        if (!warp_wait(w_full(sw), (i / RW) & 1, abort_flag, p.status)) break;
+        PS_TC_TRACE2(i, 0);
+        // the whole group landed at once: only its first k-tile waits
+        if (jj == 0 && !warp_wait(w_full(sw), (grp / WG) & 1, abort_flag, p.status)) break;
         PS_TC_TRACE(16 + (i & 255) * 8 + 5, t == 0);
+        PS_TC_TRACE2(i, 1);
+        const unsigned char* row = wring + (sw * WJ * NSUB + jj) * 8192;
+        uint4 in[kChunks];
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) in[c] = *reinterpret_cast<const uint4*>(row + (((c0 + c) ^ swz) << 4));
         if (i >= AS && !warp_wait(a_empty(sa), ((i / AS) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         PS_TC_TRACE(16 + (i & 255) * 8 + 2, t == 0);
-        const unsigned char* row = gbase + (w_addr(sw) - base) + sub * 8192 + rin * 64;
+        PS_TC_TRACE2(i, 2);
         uint32_t words[kChunks * 8];
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
-          const uint4 in = *reinterpret_cast<const uint4*>(row + (((c0 + c) ^ swz) << 4));
           uint4 lo, hi;
-          if constexpr (std::is_same<T, __half>::value) widen16_f16(in, lo, hi);
-          else widen16_bf16(in, lo, hi);
+          if constexpr (std::is_same<T, __half>::value) widen16_f16(in[c], lo, hi);
+          else widen16_bf16(in[c], lo, hi);
           words[c * 8 + 0] = lo.x; words[c * 8 + 1] = lo.y; words[c * 8 + 2] = lo.z; words[c * 8 + 3] = lo.w;
           words[c * 8 + 4] = hi.x; words[c * 8 + 5] = hi.y; words[c * 8 + 6] = hi.z; words[c * 8 + 7] = hi.w;
         }
-        const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::kAccCols + sa * C::kACols + tcol0;
+        const uint32_t ta = tlane + sa * C::kACols;
+        PS_TC_TRACE2(i, 3);
         tmem_st16(ta, words);
         if constexpr (kChunks == 4) tmem_st16(ta + 16, words + 16);
+        PS_TC_TRACE2(i, 4);
         tmem_wait_st();
+        PS_TC_TRACE2(i, 5);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(a_full(sa));
           mbar_arrive(w_empty(sw));
         }
+        PS_TC_TRACE2(i, 6);
         PS_TC_TRACE(16 + (i & 255) * 8 + 3, t == 0);
       }
     }
@@ -588,6 +649,15 @@ struct Plan {
   int nsub, bm, m_tiles, n_tiles, k_tiles, splits, per_split;
 };
 
+// PS_LINEAR_STAGGER=0 walks K in the same order in every CTA (tuning).
+bool stagger_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("PS_LINEAR_STAGGER");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 int snap_bm(int bm) { return bm <= 32 ? 32 : (bm <= 64 ? 64 : (bm <= 128 ? 128 : (bm <= 192 ? 192 : 256))); }
 
 // Tile plan (rules measured on B200 with CUDA-graph timing over the
@@ -784,6 +854,9 @@ int launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, co
 extern "C" PS_API int ps_debug_tc_trace(unsigned long long* host, int n) {
   return static_cast<int>(cudaMemcpyFromSymbol(host, g_tc_trace, sizeof(unsigned long long) * n));
 }
+extern "C" PS_API int ps_debug_tc_trace2(unsigned long long* host, int n) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_tc_trace2, sizeof(unsigned long long) * n));
+}
 #endif
 
 namespace ps_host {
@@ -841,6 +914,7 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   p.k_tiles_per_split = pl.per_split;
   p.splits = pl.splits;
   p.swiglu = swiglu ? 1 : 0;
+  p.stagger = stagger_enabled() ? 1 : 0;
   if (push) {
     // the push path stores whole 16-byte groups of outputs, residual-free
     if (resid || bias || N % 8 != 0) return PS_ERR_UNSUPPORTED;
@@ -854,7 +928,7 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   CUtensorMap wm, xm;
   bool ok = make_map(&xm, x, xdt, 2, M, K, kBK, pl.bm, CU_TENSOR_MAP_SWIZZLE_128B);
   if (int8 && w_tiled) wm = xm;  // unused: the weight arrives by contiguous bulk copies
-  else if (int8) ok = ok && make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, kBK, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else if (int8) ok = ok && make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, kBK, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
   else ok = ok && make_map(&wm, w, xdt, 2, N, K, kBK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   // Output maps (box 128 columns x BM tokens). Built whenever N % 8 == 0;
   // the kernel uses them only when the tile is not split.

@@ -44,6 +44,8 @@ PS_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // false (and raises the CTA abort flag) on timeout or when another role
 // already aborted.
 PS_DEVICE bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  // fast path: the phase is usually complete already; no clock or flag reads
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
   bool ok = true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
