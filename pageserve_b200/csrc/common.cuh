@@ -130,6 +130,15 @@ PS_DEVICE float warp_max(float v) {
 // the standalone kernel and the gate|up linear's epilogue so both give the
 // same values: g / (1 + e^-g) with the fast exponential and divide (relative
 // error ~1e-6, far below the bf16/f16 output rounding; 0 for g -> -inf).
+// Round two floats to T (round to nearest even) and back with one packed
+// convert: (float(T(a)), float(T(b))).
+template <typename T> PS_DEVICE float2 round2(float a, float b);
+template <> PS_DEVICE float2 round2<__nv_bfloat16>(float a, float b) {
+  return __bfloat1622float2(__floats2bfloat162_rn(a, b));
+}
+template <> PS_DEVICE float2 round2<__half>(float a, float b) { return __half22float2(__floats2half2_rn(a, b)); }
+template <> PS_DEVICE float2 round2<float>(float a, float b) { return make_float2(a, b); }
+
 PS_DEVICE float silu_mul_f32(float g, float u) { return __fdividef(g, 1.f + __expf(-g)) * u; }
 
 // Programmatic dependent launch (kernels launched through ps_host::launch):

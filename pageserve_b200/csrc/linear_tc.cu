@@ -52,6 +52,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "linear.cuh"
 #include "tc_ptx.cuh"
@@ -71,6 +72,11 @@ constexpr int kSmemBudget = 216 * 1024;
 #ifdef PS_TRACE
 __device__ unsigned long long g_tc_trace[4096];
 __device__ unsigned long long g_tc_trace2[4096];  // widen warp 3 lane 0, 8 points per k-tile
+#define PS_TC_TRACE3(k)                                                            \
+  do {                                                                             \
+    if (threadIdx.x == 96 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) \
+      g_tc_trace2[2048 + (k)] = clock64();                                         \
+  } while (0)
 #define PS_TC_TRACE2(i, k)                                                         \
   do {                                                                             \
     if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 256) \
@@ -82,6 +88,9 @@ __device__ unsigned long long g_tc_trace2[4096];  // widen warp 3 lane 0, 8 poin
       g_tc_trace[(slot)] = clock64();                                              \
   } while (0)
 #else
+#define PS_TC_TRACE3(k) \
+  do {                  \
+  } while (0)
 #define PS_TC_TRACE2(i, k) \
   do {                     \
   } while (0)
@@ -108,6 +117,7 @@ struct TcParams {
   int tma_out;      // splits == 1 and N % 8 == 0: outputs leave by TMA stores (OutMaps)
   int swiglu;       // rows interleaved (2i gate_i, 2i+1 up_i): y[m][i] = silu(gate) * up, width N / 2
   int stagger;      // rotate each CTA's k-tile order (see kt_of in the kernel)
+  float* ws;        // splits > 1: fp32 partial tiles [tile][split][NSUB][BM][128] in global memory (null: DSMEM)
   PushTargets push;  // world > 0: the final output goes to every rank's receive slot instead of y
 };
 
@@ -225,14 +235,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     for (int s = 0; s < WG; ++s) {
       mbar_init(w_full(s), 1);
-      mbar_init(w_empty(s), kInt8 ? kDeqWarps * WJ : 1);
+      mbar_init(w_empty(s), kInt8 ? (kDeqWarps / 2) * WJ : 1);
     }
     for (int s = 0; s < RX; ++s) {
       mbar_init(x_full(s), 1);
       mbar_init(x_empty(s), 1);
     }
     for (int s = 0; s < AS; ++s) {
-      mbar_init(a_full(s), kDeqWarps);
+      mbar_init(a_full(s), kDeqWarps / 2);
       mbar_init(a_empty(s), 1);
     }
     mbar_init(acc_full, 1);
@@ -340,52 +350,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x - 96;  // 0 .. 32*kDeqWarps-1
     (void)t;
     // ------------------------------------- int8 -> bf16 widening into TMEM --
-    // Warp (q = warp % 4, h = (warp - 3) / 4) owns TMEM lanes [32q, 32q+32):
-    // NSUB = 2: sub-tile h, the row's whole K tile (64 values, 32 columns);
-    // NSUB = 1: the row's K half h (32 values, 16 columns). Each lane reads
-    // its weight row from the (pre-swizzled) int8 stage and widens it.
+    // Warp (q = warp % 4, h = (warp - 3) / 4) owns TMEM lanes [32q, 32q+32)
+    // (one weight row per lane) and every other k-tile (parity h): each
+    // iteration widens the row's whole k-tile of every sub-tile, so the two
+    // teams' per-k-tile round trips (wait, load, widen, TMEM store, arrive)
+    // overlap instead of adding up.
     if (kInt8) {
       const int q = warp & 3;
       const int h = (warp - 3) >> 2;
       const int rin = q * 32 + lane;                        // row inside the 128-row block
-      const int sub = NSUB == 2 ? h : 0;
       const int swz = p.wt ? ((rin >> 1) & 3) : 0;           // chunk slot swizzle of the tiled layout
-      constexpr int kChunks = NSUB == 2 ? 4 : 2;             // 16-byte chunks this lane widens
-      const int c0 = NSUB == 2 ? 0 : 2 * h;
-      const uint32_t tcol0 = (NSUB == 2 ? sub * (kBK / 2) : h * (kBK / 4));
-      const unsigned char* wring = gbase + C::kOffW + (sub * WJ) * 8192 + rin * 64;
-      const uint32_t tlane = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::kAccCols + tcol0;
-      for (int i = 0; i < nkt; ++i) {
+      constexpr int kChunks = 4;                             // 16-byte chunks of one row per sub-tile
+      const unsigned char* wring = gbase + C::kOffW + rin * 64;
+      const uint32_t tlane = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::kAccCols;
+      for (int i = h; i < nkt; i += 2) {
         const int grp = i / WJ;
         const int jj = i - grp * WJ;
         const int sw = grp % WG;
         const int sa = i % AS;
         PS_TC_TRACE2(i, 0);
-        // the whole group landed at once: only its first k-tile waits
-        if (jj == 0 && !warp_wait(w_full(sw), (grp / WG) & 1, abort_flag, p.status)) break;
+        if (!warp_wait(w_full(sw), (grp / WG) & 1, abort_flag, p.status)) break;
         PS_TC_TRACE(16 + (i & 255) * 8 + 5, t == 0);
         PS_TC_TRACE2(i, 1);
-        const unsigned char* row = wring + (sw * WJ * NSUB + jj) * 8192;
-        uint4 in[kChunks];
+        // widen in registers first: only the TMEM store waits for the stage
+        uint32_t words[NSUB][kChunks * 8];
 #pragma unroll
-        for (int c = 0; c < kChunks; ++c) in[c] = *reinterpret_cast<const uint4*>(row + (((c0 + c) ^ swz) << 4));
+        for (int sub = 0; sub < NSUB; ++sub) {
+          const unsigned char* row = wring + (sw * WJ * NSUB + sub * WJ + jj) * 8192;
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            const uint4 in = *reinterpret_cast<const uint4*>(row + ((c ^ swz) << 4));
+            uint4 lo, hi;
+            if constexpr (std::is_same<T, __half>::value) widen16_f16(in, lo, hi);
+            else widen16_bf16(in, lo, hi);
+            uint32_t* w8 = words[sub] + c * 8;
+            w8[0] = lo.x; w8[1] = lo.y; w8[2] = lo.z; w8[3] = lo.w;
+            w8[4] = hi.x; w8[5] = hi.y; w8[6] = hi.z; w8[7] = hi.w;
+          }
+        }
+        PS_TC_TRACE2(i, 2);
         if (i >= AS && !warp_wait(a_empty(sa), ((i / AS) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         PS_TC_TRACE(16 + (i & 255) * 8 + 2, t == 0);
-        PS_TC_TRACE2(i, 2);
-        uint32_t words[kChunks * 8];
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          uint4 lo, hi;
-          if constexpr (std::is_same<T, __half>::value) widen16_f16(in[c], lo, hi);
-          else widen16_bf16(in[c], lo, hi);
-          words[c * 8 + 0] = lo.x; words[c * 8 + 1] = lo.y; words[c * 8 + 2] = lo.z; words[c * 8 + 3] = lo.w;
-          words[c * 8 + 4] = hi.x; words[c * 8 + 5] = hi.y; words[c * 8 + 6] = hi.z; words[c * 8 + 7] = hi.w;
-        }
-        const uint32_t ta = tlane + sa * C::kACols;
         PS_TC_TRACE2(i, 3);
-        tmem_st16(ta, words);
-        if constexpr (kChunks == 4) tmem_st16(ta + 16, words + 16);
+#pragma unroll
+        for (int sub = 0; sub < NSUB; ++sub) {
+          const uint32_t ta = tlane + sa * C::kACols + sub * (kBK / 2);
+          tmem_st16(ta, words[sub]);
+          tmem_st16(ta + 16, words[sub] + 16);
+        }
         PS_TC_TRACE2(i, 4);
         tmem_wait_st();
         PS_TC_TRACE2(i, 5);
@@ -446,7 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
           for (int c = 32 * h; c < BM; c += 64) {
             float v[32];
+            PS_TC_TRACE3(sub * 32 + (c / 64) * 4 + 0);
             if (ok) tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
+            PS_TC_TRACE3(sub * 32 + (c / 64) * 4 + 1);
             if (use_tma && p.swiglu) {
               // lanes 2k / 2k+1 hold gate / up of intermediate channel
               // (n0 + sub*128 + q*32)/2 + k: each rounded to dtype (the
@@ -454,16 +469,25 @@ __global__ void __launch_bounds__(kThreads, 1)
               T* tile2 = out_tile + sub * BM * 64;  // [BM][64] per sub-tile
               // The pair splits the 32 tokens: the even lane finishes tokens
               // 0..15, the odd lane 16..31 (one exchange per token pair).
+              // Written as independent batches (round all, exchange all,
+              // SiLU all, store all): one output's chain of ~15 dependent
+              // steps is far longer than its instruction count.
               const bool odd = lane & 1;
+              float keep[16], send[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const float mine_lo = to_f32(from_f32<T>(v[j] * sc + bs));
-                const float mine_hi = to_f32(from_f32<T>(v[j + 16] * sc + bs));
-                const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_lo : mine_hi, 1);
-                const float gate = odd ? other : mine_lo;
-                const float up = odd ? mine_hi : other;
-                tile2[(c + j + (odd ? 16 : 0)) * 64 + q * 16 + (lane >> 1)] = from_f32<T>(silu_mul_f32(gate, up));
+                // both values rounded to the linear's dtype by one packed convert
+                const float2 r = round2<T>(v[j] * sc + bs, v[j + 16] * sc + bs);
+                keep[j] = odd ? r.y : r.x;
+                send[j] = odd ? r.x : r.y;
               }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) send[j] = __shfl_xor_sync(0xffffffffu, send[j], 1);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) keep[j] = odd ? silu_mul_f32(send[j], keep[j]) : silu_mul_f32(keep[j], send[j]);
+              T* col = tile2 + (c + (odd ? 16 : 0)) * 64 + q * 16 + (lane >> 1);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) col[j * 64] = from_f32<T>(keep[j]);
             } else if (use_tma) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -484,9 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+          PS_TC_TRACE3(sub * 32 + 20);
           if (use_tma) {
             fence_proxy_async();
             epi_bar();
+            PS_TC_TRACE3(sub * 32 + 21);
             if (threadIdx.x == 96) {
               if (p.swiglu) {
                 tma_store_2d(&om.y, out_sa + sub * BM * 128, (n0 + sub * 128) / 2, m0);
@@ -505,8 +531,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        PS_TC_TRACE3(100);
         if (use_tma && threadIdx.x == 96) {
           bulk_wait_all();  // stores done (pushed outputs complete before the arrival below)
+          PS_TC_TRACE3(101);
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
       }
@@ -521,8 +549,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r1 = min(BM, r0 + share);
       const int my_rows = r1 - r0;
       const int ndst = p.push.world > 0 ? p.push.world : 1;
+      // With a workspace the splits exchange their partial tiles through L2:
+      // each stages its fp32 tile in shared memory and writes it to its
+      // workspace slot with one bulk store; a GPU-scope fence and the cluster
+      // barrier publish them, and each CTA sums its token-row slice over the
+      // splits in split order (ld.cg, all splits' loads in flight at once).
+      // Bulk copies between the CTAs' shared memories (the fallback without
+      // a workspace) measured ~13 GB/s per SM on B200, several us per tile.
+      const long long tile = static_cast<long long>(blockIdx.y) * gridDim.x + blockIdx.x;
+      auto part = [&](int sr, int sub_) {
+        return p.ws + ((tile * S + sr) * NSUB + sub_) * static_cast<long long>(BM) * 128;
+      };
 #pragma unroll 1
       for (int sub = 0; sub < NSUB; ++sub) {
+        // thread t sums columns n8 = 8 * (t % 16) of the sub-tile, 22 rows per
+        // pass; its scales and biases are requested before the exchange
+        const int n8 = (threadIdx.x & 15) * 8;
+        const int gn = n0 + sub * 128 + n8;
+        const int cnt = min(8, p.N - gn);
+        float sc[8], bs[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          sc[j] = (j < cnt && p.scale) ? p.scale[gn + j] : 1.f;
+          bs[j] = (j < cnt && bias) ? to_f32(bias[gn + j]) : 0.f;
+        }
         if (warp >= 3 && ok) {
 #pragma unroll 1
           for (int c = 32 * h; c < BM; c += 64) {
@@ -532,35 +582,117 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) stage[(c + j) * 128 + q * 32 + lane] = v[j];
           }
         }
-        fence_proxy_async();  // generic stage writes -> the bulk copies below
-        if (threadIdx.x == 96) mbar_expect_tx(recv_full, (S - 1) * my_rows * 512);
-        PS_TC_TRACE(5 + sub * 4, threadIdx.x == 96);
-        cluster_sync();  // every split staged; every peer's rings idle
-        PS_TC_TRACE(6 + sub * 4, threadIdx.x == 96);
-        if (threadIdx.x == 96) {
-          for (int j = 0; j < S; ++j) {
-            if (j == crank) continue;
+        if (p.ws) {
+          fence_proxy_async();  // generic stage writes -> the bulk stores
+          __syncthreads();
+          // publish only the row slices the peers own (this CTA's own rows
+          // stay in shared memory); slice j leaves from lane 0 of warp 3 + j
+          if (lane == 0 && warp >= 3 && warp - 3 < S && warp - 3 != crank) {
+            const int j0 = min(BM, (warp - 3) * share);
+            const int rows = min(BM, j0 + share) - j0;
+            if (rows > 0) {
+              bulk_store(part(crank, sub) + j0 * 128, stage_sa + j0 * 512, rows * 512);
+              bulk_commit();
+              bulk_wait_all();
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+          }
+          __threadfence();
+          PS_TC_TRACE(5 + sub * 4, threadIdx.x == 96);
+          cluster_sync();  // every split's partial tile is in L2
+          PS_TC_TRACE(6 + sub * 4, threadIdx.x == 96);
+        } else {
+          fence_proxy_async();  // generic stage writes -> the bulk copies below
+          if (threadIdx.x == 96) mbar_expect_tx(recv_full, (S - 1) * my_rows * 512);
+          PS_TC_TRACE(5 + sub * 4, threadIdx.x == 96);
+          cluster_sync();  // every split staged; every peer's rings idle
+          PS_TC_TRACE(6 + sub * 4, threadIdx.x == 96);
+          // the copy to peer j leaves from lane 0 of warp 3 + j: a thread issues
+          // about one bulk copy per ~700 cycles, so one thread for all S - 1
+          // copies would serialise them
+          if (lane == 0 && warp >= 3 && warp - 3 < S && warp - 3 != crank) {
+            const int j = warp - 3;
             const int j0 = min(BM, j * share);
             const int rows = min(BM, j0 + share) - j0;
-            if (rows <= 0) continue;
-            const int slot = crank < j ? crank : crank - 1;  // my slot among j's S-1 senders
-            bulk_s2s(mapa_shared(recv_sa + slot * share * 512, j), stage_sa + j0 * 512, rows * 512,
-                     mapa_shared(recv_full, j));
+            if (rows > 0) {
+              const int slot = crank < j ? crank : crank - 1;  // my slot among j's S-1 senders
+              bulk_s2s(mapa_shared(recv_sa + slot * share * 512, j), stage_sa + j0 * 512, rows * 512,
+                       mapa_shared(recv_full, j));
+            }
           }
         }
-        const bool got = warp_wait(recv_full, sub & 1, abort_flag, p.status);
-        // thread t owns columns n8 = 8 * (t % 16) of the sub-tile, 22 rows per pass
-        const int n8 = (threadIdx.x & 15) * 8;
-        const int gn = n0 + sub * 128 + n8;
+        const bool got = p.ws ? true : warp_wait(recv_full, sub & 1, abort_flag, p.status);
         if (got && gn < p.N) {
-          const int cnt = min(8, p.N - gn);
           const bool vec = (p.N % 8) == 0;
-          float sc[8], bs[8];
+          // L2 path, full 16-byte groups: the residual and every split's
+          // partial are requested before any is summed (each pass is one round
+          // trip to L2 instead of S + 1).
+          constexpr int kRowStep = kThreads / 16;
+          // rows per pass sized to the split count (registers: R x SMAX x 32 B)
+          auto l2_rows = [&](auto RT, auto ST) {
+            constexpr int R = decltype(RT)::value;
+            constexpr int SMAX = decltype(ST)::value;
+#pragma unroll 1
+            for (int m = r0 + (threadIdx.x >> 4); m < r1; m += R * kRowStep) {
+              float4 pa[R][SMAX], pb[R][SMAX];
+              uint4 rres[R];
+              bool live[R];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            sc[j] = (j < cnt && p.scale) ? p.scale[gn + j] : 1.f;
-            bs[j] = (j < cnt && bias) ? to_f32(bias[gn + j]) : 0.f;
-          }
+              for (int u = 0; u < R; ++u) {
+                const int mm = m + u * kRowStep;
+                live[u] = mm < r1 && m0 + mm < p.M;
+                rres[u] = make_uint4(0, 0, 0, 0);
+                if (!live[u]) continue;
+                if (resid) rres[u] = *reinterpret_cast<const uint4*>(resid + static_cast<long long>(m0 + mm) * p.N + gn);
+#pragma unroll
+                for (int sr = 0; sr < SMAX; ++sr) {
+                  if (sr < S) {
+                    const float4* src = sr == crank ? reinterpret_cast<const float4*>(stage + mm * 128 + n8)
+                                                    : reinterpret_cast<const float4*>(part(sr, sub) + mm * 128 + n8);
+                    pa[u][sr] = sr == crank ? src[0] : __ldcg(src);
+                    pb[u][sr] = sr == crank ? src[1] : __ldcg(src + 1);
+                  }
+                }
+              }
+              PS_TC_TRACE3(102 + min(7, (m - r0) / (R * kRowStep)) * 2);
+#pragma unroll
+              for (int u = 0; u < R; ++u) {
+                if (!live[u]) continue;
+                const int gm = m0 + m + u * kRowStep;
+                float acc[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+                for (int sr = 0; sr < SMAX; ++sr) {  // split order: identical sums on every run
+                  if (sr < S) {
+                    acc[0] += pa[u][sr].x; acc[1] += pa[u][sr].y; acc[2] += pa[u][sr].z; acc[3] += pa[u][sr].w;
+                    acc[4] += pb[u][sr].x; acc[5] += pb[u][sr].y; acc[6] += pb[u][sr].z; acc[7] += pb[u][sr].w;
+                  }
+                }
+                float rv[8];
+                if (resid) unpack8<T>(rres[u], rv);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  acc[j] = acc[j] * sc[j] + bs[j];
+                  if (resid) acc[j] = to_f32(from_f32<T>(acc[j])) + rv[j];
+                }
+                const uint4 pk = pack8<T>(acc);
+                const long long off = static_cast<long long>(gm) * p.N + gn;
+                if (p.push.world > 0 && p.push.slice) {  // two-shot: the owner of these columns only
+                  const int d = gn / p.push.slice;
+                  *reinterpret_cast<uint4*>(static_cast<T*>(p.push.dst[d]) + push_offset(p.push, gm, gn, p.N, d)) = pk;
+                } else {
+                  for (int d = 0; d < ndst; ++d)  // push: every rank's slot (peers over NVLink)
+                    *reinterpret_cast<uint4*>((p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off) = pk;
+                }
+              }
+              PS_TC_TRACE3(103 + min(7, (m - r0) / (R * kRowStep)) * 2);
+            }
+          };
+          if (p.ws && vec) {
+            if (S <= 2) l2_rows(std::integral_constant<int, 2>{}, std::integral_constant<int, 2>{});
+            else l2_rows(std::integral_constant<int, 1>{}, std::integral_constant<int, 8>{});
+          } else {
 #pragma unroll 1
           for (int m = r0 + (threadIdx.x >> 4); m < r1; m += kThreads / 16) {
             const int gm = m0 + m;
@@ -568,14 +700,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             float acc[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-            for (int sr = 0; sr < S; ++sr) {  // split order: identical sums on every run
-              const float* src = sr == crank ? stage + m * 128 + n8
-                                             : reinterpret_cast<const float*>(gbase + C::kOffStage + BM * 512) +
-                                                   ((sr < crank ? sr : sr - 1) * share + (m - r0)) * 128 + n8;
-              const float4 a = reinterpret_cast<const float4*>(src)[0];
-              const float4 b = reinterpret_cast<const float4*>(src)[1];
-              acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-              acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+            if (p.ws) {
+              for (int sr = 0; sr < S; ++sr) {  // split order: identical sums on every run
+                const float4* src = sr == crank ? reinterpret_cast<const float4*>(stage + m * 128 + n8)
+                                                : reinterpret_cast<const float4*>(part(sr, sub) + m * 128 + n8);
+                const float4 a = sr == crank ? src[0] : __ldcg(src);
+                const float4 b = sr == crank ? src[1] : __ldcg(src + 1);
+                acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+                acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+              }
+            } else {
+              for (int sr = 0; sr < S; ++sr) {  // split order: identical sums on every run
+                const float* src = sr == crank ? stage + m * 128 + n8
+                                               : reinterpret_cast<const float*>(gbase + C::kOffStage + BM * 512) +
+                                                     ((sr < crank ? sr : sr - 1) * share + (m - r0)) * 128 + n8;
+                const float4 a = reinterpret_cast<const float4*>(src)[0];
+                const float4 b = reinterpret_cast<const float4*>(src)[1];
+                acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+                acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+              }
             }
             const long long off = static_cast<long long>(gm) * p.N + gn;
             if (vec) {
@@ -605,9 +748,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+          }
         }
         PS_TC_TRACE(7 + sub * 4, threadIdx.x == 96);
-        cluster_sync();  // slices consumed, stage and receive buffers free again
+        // slices consumed: stage and receive buffers free again (the L2 path
+        // writes each sub-tile's partials to slots of their own, so only this
+        // CTA's stage must be released)
+        if (p.ws) __syncthreads();
+        else cluster_sync();
         PS_TC_TRACE(8 + sub * 4, threadIdx.x == 96);
       }
     }
@@ -738,8 +886,14 @@ Plan plan(int M, int N, int K, bool int8) {
   return pl;
 }
 
+// Bytes of the split-K partial-tile exchange for `splits` splits.
+size_t split_ws_bytes(const Plan& pl, int splits) {
+  return splits > 1 ? static_cast<size_t>(pl.n_tiles) * pl.m_tiles * splits * pl.nsub * pl.bm * 128 * 4 : 0;
+}
+
 template <typename T, bool kInt8, int NSUB, int BM>
-int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl, const OutMaps& om, cudaStream_t s) {
+int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl, const OutMaps& om, cudaStream_t s,
+               void* ws, size_t ws_bytes) {
   using C = Cfg<kInt8, NSUB, BM>;
   auto kern = linear_tc_kernel<T, kInt8, NSUB, BM>;
   static bool attr_set = false;  // one attribute call per instantiation
@@ -750,12 +904,8 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl
     }
     attr_set = true;
   }
-  // split-K: the fp32 stage plus S-1 received row slices must fit the rings
   int splits = pl.splits;
-  while (splits > 1 && static_cast<long long>(BM) * 512 + static_cast<long long>(splits - 1) *
-                                                             ((BM + splits - 1) / splits) * 512 > C::kRings)
-    --splits;
-  // ... and all clusters must be resident at once: a cluster needs `splits`
+  // split-K: all clusters must be resident at once: a cluster needs `splits`
   // SMs of one GPC, so large clusters can leave a second wave (queried once
   // per cluster size from the occupancy calculator).
   static int max_clusters[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
@@ -782,6 +932,17 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl
     }
     if (max_clusters[splits] >= tiles) break;
     --splits;
+  }
+  // the partial tiles go through the caller's workspace when it is large
+  // enough; otherwise through shared memory, where the fp32 stage plus S-1
+  // received row slices must fit the rings
+  p.ws = nullptr;
+  if (splits > 1 && ws && ws_bytes >= split_ws_bytes(pl, splits) && ps_host::aligned(ws, 16)) {
+    p.ws = static_cast<float*>(ws);
+  } else {
+    while (splits > 1 && static_cast<long long>(BM) * 512 + static_cast<long long>(splits - 1) *
+                                                               ((BM + splits - 1) / splits) * 512 > C::kRings)
+      --splits;
   }
   if (splits != pl.splits) {
     pl.per_split = (pl.k_tiles + splits - 1) / splits;
@@ -828,24 +989,25 @@ int launch_cfg(const CUtensorMap& wm, const CUtensorMap& xm, TcParams p, Plan pl
 
 template <typename T, bool kInt8, int NSUB>
 int launch_nsub(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, const OutMaps& om,
-                cudaStream_t s) {
+                cudaStream_t s, void* ws, size_t wsb) {
   switch (pl.bm) {
-    case 32: return launch_cfg<T, kInt8, NSUB, 32>(wm, xm, p, pl, om, s);
-    case 64: return launch_cfg<T, kInt8, NSUB, 64>(wm, xm, p, pl, om, s);
-    case 128: return launch_cfg<T, kInt8, NSUB, 128>(wm, xm, p, pl, om, s);
-    case 192: return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, om, s);
+    case 32: return launch_cfg<T, kInt8, NSUB, 32>(wm, xm, p, pl, om, s, ws, wsb);
+    case 64: return launch_cfg<T, kInt8, NSUB, 64>(wm, xm, p, pl, om, s, ws, wsb);
+    case 128: return launch_cfg<T, kInt8, NSUB, 128>(wm, xm, p, pl, om, s, ws, wsb);
+    case 192: return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, om, s, ws, wsb);
     default:
       // int8 with 256-row slabs caps the token tile at 192 (TMEM holds the
       // accumulators and two widened A stages); the planner never asks more.
-      if constexpr (kInt8 && NSUB == 2) return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, om, s);
-      else return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, om, s);
+      if constexpr (kInt8 && NSUB == 2) return launch_cfg<T, kInt8, NSUB, 192>(wm, xm, p, pl, om, s, ws, wsb);
+      else return launch_cfg<T, kInt8, NSUB, 256>(wm, xm, p, pl, om, s, ws, wsb);
   }
 }
 
 template <typename T, bool kInt8>
 int launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, const Plan& pl, const OutMaps& om,
-             cudaStream_t s) {
-  return pl.nsub == 2 ? launch_nsub<T, kInt8, 2>(wm, xm, p, pl, om, s) : launch_nsub<T, kInt8, 1>(wm, xm, p, pl, om, s);
+             cudaStream_t s, void* ws, size_t wsb) {
+  return pl.nsub == 2 ? launch_nsub<T, kInt8, 2>(wm, xm, p, pl, om, s, ws, wsb)
+                      : launch_nsub<T, kInt8, 1>(wm, xm, p, pl, om, s, ws, wsb);
 }
 
 }  // namespace
@@ -861,7 +1023,18 @@ extern "C" PS_API int ps_debug_tc_trace2(unsigned long long* host, int n) {
 
 namespace ps_host {
 
-size_t linear_tc_workspace(int, int, int) { return 0; }  // split-K reduces on chip (clusters)
+// Split-K partial-tile exchange (an upper bound: the launch may use fewer
+// splits). Without it the splits reduce through shared memory, slower.
+size_t linear_tc_workspace(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  size_t b = 0;
+  for (bool int8 : {true, false}) {
+    const Plan pl = plan(M, N, K, int8);
+    const size_t v = split_ws_bytes(pl, pl.splits);
+    if (v > b) b = v;
+  }
+  return b;
+}
 
 size_t tiled_int8_bytes(int N, int K) {
   return static_cast<size_t>((N + 127) / 128) * ((K + kBK - 1) / kBK) * 8192;
@@ -920,8 +1093,6 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
     if (resid || bias || N % 8 != 0) return PS_ERR_UNSUPPORTED;
     p.push = *push;
   }
-  (void)workspace;
-  (void)workspace_bytes;
   const CUtensorMapDataType xdt =
       dtype == PS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int bn = 128 * pl.nsub;
@@ -951,9 +1122,12 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
     set_error("linear: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
     return PS_ERR_CUDA;
   }
+  void* ws = workspace;
+  const size_t wsb = workspace_bytes;
   if (dtype == PS_BF16)
-    return int8 ? launch_t<__nv_bfloat16, true>(wm, xm, p, pl, om, s) : launch_t<__nv_bfloat16, false>(wm, xm, p, pl, om, s);
-  return int8 ? launch_t<__half, true>(wm, xm, p, pl, om, s) : launch_t<__half, false>(wm, xm, p, pl, om, s);
+    return int8 ? launch_t<__nv_bfloat16, true>(wm, xm, p, pl, om, s, ws, wsb)
+                : launch_t<__nv_bfloat16, false>(wm, xm, p, pl, om, s, ws, wsb);
+  return int8 ? launch_t<__half, true>(wm, xm, p, pl, om, s, ws, wsb) : launch_t<__half, false>(wm, xm, p, pl, om, s, ws, wsb);
 }
 
 }  // namespace ps_host

@@ -87,6 +87,12 @@ PS_DEVICE void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) 
                "r"(src), "r"(x), "r"(y)
                : "memory");
 }
+// Contiguous shared -> global bulk store (bulk async-group; 16-byte aligned,
+// size a multiple of 16).
+PS_DEVICE void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
 PS_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 PS_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 PS_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

@@ -50,10 +50,11 @@ def dequantize(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torc
 
 
 class LinearWorkspace:
-    """Grow-only scratch buffer for the split-K reduction of the tensor-core
-    linear: arrival counters and float32 partial sums. It must start zeroed;
-    every kernel call leaves the part it used zeroed again, so one buffer is
-    reused by all the linears of a step (calls on one stream only)."""
+    """Grow-only scratch buffer of the tensor-core linear: the float32
+    partial tiles that the split-K CTAs of an output tile exchange through L2
+    (each call writes every slot it reads, so no clearing is needed). One
+    buffer serves all the linears of a step (calls on one stream only);
+    without it the splits reduce through shared memory, more slowly."""
 
     def __init__(self):
         self.buf: torch.Tensor | None = None

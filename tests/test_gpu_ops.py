@@ -373,6 +373,44 @@ def test_w8a16_linear_tiled_matches_oracle(dev, M, NK):
     assert rel_err(y.float().cpu().numpy(), ref) < REL_TOL
 
 
+@pytest.mark.parametrize("MNK", [(576, 2560, 2048), (576, 2048, 11008), (130, 2048, 5504), (256, 300, 8192)])
+def test_split_k_exchange_paths_agree(dev, MNK):
+    """Split-K tiles reduce their partial sums through the caller's workspace
+    (L2) or, without one, through the cluster's shared memories: both sum
+    the splits in the same order, so the outputs are bit-identical, and both
+    match the oracle."""
+    import ctypes
+
+    from pageserve_b200 import _lib
+    from pageserve_b200.quantization import tile_int8_weight
+    M, N, K = MNK
+    lib = _lib.load()
+    rng = np.random.default_rng(M + N + K)
+    q = rng.integers(-127, 128, size=(N, K)).astype(np.int8)
+    scale = rng.uniform(1e-3, 1e-2, size=(N, 1)).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    r = rng.standard_normal((M, N), dtype=np.float32)
+    qt = tile_int8_weight(torch.from_numpy(q).to(dev))
+    xd, rd = _bf16(x, dev), _bf16(r, dev)
+    sd = torch.from_numpy(scale).to(dev)
+    need = lib.ps_w8a16_linear_tiled_workspace_size(M, N, K)
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    outs = []
+    for wsp, wsb in ((ws.data_ptr(), need), (None, 0)):
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        for _ in range(2):
+            rc = lib.ps_w8a16_linear_tiled(y.data_ptr(), xd.data_ptr(), qt.data_ptr(), sd.data_ptr(), None,
+                                           rd.data_ptr(), M, N, K, _lib.PS_BF16, wsp, ctypes.c_size_t(wsb),
+                                           _lib.stream_ptr(dev))
+            assert rc == 0, _lib.last_error()
+        torch.cuda.synchronize()
+        outs.append(y)
+    _lib.raise_on_device_error()
+    assert torch.equal(outs[0], outs[1])
+    ref = ops.quantized_linear(ops.round_bf16(x), q, scale, None) + ops.round_bf16(r)
+    assert rel_err(outs[0].float().cpu().numpy(), ref) < REL_TOL
+
+
 @pytest.mark.parametrize("M", [1, 7, 64, 576])
 @pytest.mark.parametrize("IK", [(11008, 2048), (160, 256), (1376, 2048), (896, 640)])
 def test_linear_swiglu_matches_oracle(dev, M, IK):
