@@ -14,6 +14,7 @@
 // its logical MMA positions (2c, 2c+1, 2c+8, 2c+9) hold physical
 // (16c+4s .. 16c+4s+3), in both A (weights) and B (activations), so every
 // lane issues whole 16-byte loads and no data moves between lanes.
+#include <cstdlib>
 #include <cstring>
 
 #include "linear.cuh"
@@ -185,6 +186,16 @@ __global__ void __launch_bounds__(W * 32) linear_mma_kernel(
   if (push.world > 0) push_arrive(push);
 }
 
+// k-tiles of weight loads each warp keeps in flight (PS_MMA_DEPTH = 2, 4 or
+// 8 overrides the default for tuning).
+int mma_depth() {
+  static const int v = [] {
+    const char* e = std::getenv("PS_MMA_DEPTH");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 template <typename T, int W>
 int launch_w(void* y, const void* x, const int8_t* q, bool tiled, const float* scale, const void* bias,
              const void* resid, int M, int N, int K, bool swiglu, const PushTargets& pt, cudaStream_t s) {
@@ -206,8 +217,12 @@ int launch_w(void* y, const void* x, const int8_t* q, bool tiled, const float* s
     return dim3(groups < per_sm ? groups : per_sm);
   };
 #define PS_MMA_LAUNCH(NT)                                                                                         \
+  if (mma_depth() >= 8) PS_MMA_LAUNCH_D(NT, 8)                                                                    \
+  else if (mma_depth() >= 4 || W > 8) PS_MMA_LAUNCH_D(NT, 4)                                                      \
+  else PS_MMA_LAUNCH_D(NT, 2)
+#define PS_MMA_LAUNCH_D(NT, DEPTH)                                                                                \
   {                                                                                                               \
-    auto kern = linear_mma_kernel<T, NT, W, (W > 8 ? 4 : 2)>;                                                     \
+    auto kern = linear_mma_kernel<T, NT, W, DEPTH>;                                                               \
     ps_host::launch(kern, grid_for(kern), W * 32, 0, s, static_cast<T*>(y), static_cast<const T*>(x), q, tiled ? 1 : 0, scale, \
                                            static_cast<const T*>(bias), static_cast<const T*>(resid), M, N, K,    \
                                            swiglu ? 1 : 0, pt);                                                   \
@@ -216,6 +231,7 @@ int launch_w(void* y, const void* x, const int8_t* q, bool tiled, const float* s
   else if (M <= 16) PS_MMA_LAUNCH(2)
   else PS_MMA_LAUNCH(4)
 #undef PS_MMA_LAUNCH
+#undef PS_MMA_LAUNCH_D
   ps_host::count_launch();
   return ps_host::check_launch("linear_mma");
 }
