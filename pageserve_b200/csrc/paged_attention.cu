@@ -189,10 +189,12 @@ template <int D>
 struct CpAsyncLayout {  // [key][D] rows, chunk ^ (row & 7) swizzle (cp.async staging)
   static PS_DEVICE uint32_t addr(int row, int chunk) { return swz(row, chunk, D * 2); }
 };
-struct TmaLayout {  // D = 128 tiles of 16-key blocks, each as two 128B-swizzled [16 keys][64] halves (TMA)
+// D = 128 tiles of 16-key blocks, each block one 4 KB TMA box [16 keys][2 halves][64]
+// (128B swizzle: the 16-byte chunk index is XORed with the 128-byte line index mod 8).
+struct TmaLayout {
   static PS_DEVICE uint32_t addr(int row, int chunk) {
-    return static_cast<uint32_t>((row >> 4) * 4096 + (chunk >> 3) * 2048 + (row & 15) * 128 +
-                                 (((chunk & 7) ^ (row & 7)) << 4));
+    const int line = (row & 15) * 2 + (chunk >> 3);
+    return static_cast<uint32_t>((row >> 4) * 4096 + line * 128 + (((chunk & 7) ^ (line & 7)) << 4));
   }
 };
 
@@ -596,11 +598,13 @@ __global__ void __launch_bounds__(kThreads) paged_attention_kernel(const AttnPar
 // TMA-fed decode kernel for the serving shape (head_dim 128, block size 16).
 // CTA = (context split, kv head, sequence), 5 warps: warp 0 produces, warps
 // 1..4 consume. The producer looks up each 16-key block of a 64-key tile in
-// the block table and issues 3-D TMA loads (box: 64 dims x 1 head x 16 keys,
-// 128B swizzle) of its K and V halves into a 3-stage mbarrier ring; consumer
-// warp w owns block w-1 of every tile (one 16-key mma.sync slab). Loads are
-// a handful of instructions per 8 KB, so the ring keeps ~2 tiles per CTA (2
-// CTAs per SM) in flight.
+// the block table and issues one 4-D TMA load per block for K and one for V
+// (box: 64 dims x 2 halves x 1 head x 16 keys = 4 KB, 128B swizzle) into a
+// 3-stage mbarrier ring; consumer warp w owns block w-1 of every tile (one
+// 16-key mma.sync slab). A thread issues TMA loads at a bounded rate whatever
+// their size, so whole-block boxes (rather than one per D half) keep the
+// producer ahead of the HBM stream; the ring holds ~2 tiles per CTA (2 CTAs
+// per SM) in flight.
 constexpr int kTmaStages = 3;
 constexpr int kTmaTile = 64;
 constexpr int kTmaStageBytes = 2 * kTmaTile * 128 * 2;  // K + V, 32 KB
@@ -643,6 +647,13 @@ PS_DEVICE bool warp_wait_a(uint32_t bar, uint32_t parity, volatile int* abort_fl
     }
   }
   return __all_sync(0xffffffffu, ok);
+}
+PS_DEVICE void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
 }
 PS_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
   asm volatile(
@@ -755,10 +766,9 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
             phys = 0;  // keep the transaction count; the output is flagged invalid
           }
           const int row = phys * 16;
-          tma_load_3d(kst + j * 4096, &kmap, full(s), 0, h, row);
-          tma_load_3d(kst + j * 4096 + 2048, &kmap, full(s), 64, h, row);
-          tma_load_3d(vst + j * 4096, &vmap, full(s), 0, h, row);
-          tma_load_3d(vst + j * 4096 + 2048, &vmap, full(s), 64, h, row);
+          // one 4 KB box per block and tensor (both D halves of kv head h)
+          tma_load_4d(kst + j * 4096, &kmap, full(s), 0, 0, h, row);
+          tma_load_4d(vst + j * 4096, &vmap, full(s), 0, 0, h, row);
         }
       }
       __syncwarp();
@@ -794,8 +804,7 @@ __global__ void __launch_bounds__(160) decode_tma_kernel(const __grid_constant__
           unsigned char* vb = gbase + (vst - base) + cw * 4096;
           for (int u = lane; u < (16 - valid) * 16; u += 32) {
             const int row = valid + u / 16, part = u % 16;
-            *reinterpret_cast<uint4*>(vb + (part >> 3) * 2048 + row * 128 + ((part & 7) << 4)) =
-                make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vb + row * 256 + part * 16) = make_uint4(0, 0, 0, 0);  // whole rows
           }
           __syncwarp();
         }
@@ -1354,6 +1363,22 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
 
 // One layer's cache as a 3-D tensor [num_blocks*16 keys][Hkv][128] with a
 // 64 x 1 x 16 box (one half of one head's 16-key block), 128B swizzle.
+// The KV cache as a 4-D tensor {64 dims, 2 halves, Hkv, NB*16 rows}: one box
+// {64, 2, 1, 16} = 4 KB loads a whole 16-key block of one kv head (both D
+// halves, 128B swizzle per 128-byte line) in a single TMA.
+bool make_kv_map4(CUtensorMap* map, const void* cache, bool bf16, int num_blocks, int Hkv) {
+  auto fn = attn_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {64, 2, static_cast<cuuint64_t>(Hkv), static_cast<cuuint64_t>(num_blocks) * 16};
+  cuuint64_t strides[3] = {64 * 2, 128 * 2, static_cast<cuuint64_t>(Hkv) * 128 * 2};
+  cuuint32_t box[4] = {64, 2, 1, 16};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+            const_cast<void*>(cache), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_kv_map(CUtensorMap* map, const void* cache, bool bf16, int num_blocks, int Hkv) {
   auto fn = attn_encode_fn();
   if (!fn) return false;
@@ -1371,7 +1396,8 @@ template <typename T>
 int launch_decode_tma(AttnParams& p, int num_seqs, int max_q_len, cudaStream_t s) {
   CUtensorMap km, vm;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-  if (!make_kv_map(&km, p.k_cache, bf16, p.num_blocks, p.Hkv) || !make_kv_map(&vm, p.v_cache, bf16, p.num_blocks, p.Hkv)) {
+  if (!make_kv_map4(&km, p.k_cache, bf16, p.num_blocks, p.Hkv) ||
+      !make_kv_map4(&vm, p.v_cache, bf16, p.num_blocks, p.Hkv)) {
     ps_host::set_error("paged_attention: cuTensorMapEncodeTiled failed for the KV cache");
     return PS_ERR_CUDA;
   }
