@@ -12,13 +12,6 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
               const void* resid, int M, int N, int K, int dtype, void* workspace, size_t workspace_bytes,
               cudaStream_t s, const int8_t* w_tiled = nullptr, const ps::PushTargets* push = nullptr,
               bool swiglu = false);
-// tcgen05 CTA-pair kernel (cta_group::2, persistent, double-buffered TMEM
-// accumulators) for pre-tiled int8 weights, N % 256 == 0 and enough
-// 256 x BM tiles to fill the GPU; PS_TC2=0 disables it, PS_TC2=2 forces it
-// wherever it is legal.
-bool linear_tc2_eligible(int M, int N, int K, bool int8, const int8_t* w_tiled, bool push, int dtype);
-int linear_tc2(void* y, const void* x, const int8_t* w_tiled, const float* scale, const void* bias,
-               const void* resid, int M, int N, int K, int dtype, cudaStream_t s, bool swiglu);
 // int8 weight re-tiled into 8 KB blocks [N/128][K/64][128][64] for linear_tc.
 size_t tiled_int8_bytes(int N, int K);
 int tile_int8(int8_t* dst, const int8_t* src, int N, int K, cudaStream_t s);

@@ -1058,10 +1058,6 @@ int linear_tc(void* y, const void* x, const void* w, int wdtype, const float* sc
   if (swiglu && (resid || push || N % 16 != 0)) return PS_ERR_UNSUPPORTED;
   const bool int8 = wdtype == PS_I8;
   if (!int8 && wdtype != dtype) return PS_ERR_UNSUPPORTED;
-  if (linear_tc2_eligible(M, N, K, int8, w_tiled, push != nullptr, dtype)) {
-    const int rc = linear_tc2(y, x, w_tiled, scale, bias, resid, M, N, K, dtype, s, swiglu);
-    if (rc != PS_ERR_UNSUPPORTED) return rc;
-  }
   // TMA: global row strides must be multiples of 16 bytes; the epilogue's
   // vector loads of scale/bias/residual need 16-byte alignment.
   if (K % 16 != 0 || !aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !aligned(resid, 16) ||

@@ -1,5 +1,5 @@
-// Inline-PTX building blocks of the tcgen05 GEMM kernels (linear_tc.cu,
-// linear_tc2.cu): mbarriers with bounded waits, TMA / bulk copies, cluster
+// Inline-PTX building blocks of the tcgen05 GEMM kernel (linear_tc.cu):
+// mbarriers with bounded waits, TMA / bulk copies, cluster
 // addressing, shared-memory matrix and instruction descriptors, tcgen05 MMA,
 // commit and TMEM load/store, and the host-side tensor-map encoder.
 #pragma once
