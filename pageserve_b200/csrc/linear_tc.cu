@@ -71,29 +71,12 @@ constexpr int kSmemBudget = 216 * 1024;
 // only with -DPS_TRACE (never in the shipped library).
 #ifdef PS_TRACE
 __device__ unsigned long long g_tc_trace[4096];
-__device__ unsigned long long g_tc_trace2[4096];  // widen warp 3 lane 0, 8 points per k-tile
-#define PS_TC_TRACE3(k)                                                            \
-  do {                                                                             \
-    if (threadIdx.x == 96 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) \
-      g_tc_trace2[2048 + (k)] = clock64();                                         \
-  } while (0)
-#define PS_TC_TRACE2(i, k)                                                         \
-  do {                                                                             \
-    if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 256) \
-      g_tc_trace2[(i) * 8 + (k)] = clock64();                                      \
-  } while (0)
 #define PS_TC_TRACE(slot, cond)                                                    \
   do {                                                                             \
     if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)           \
       g_tc_trace[(slot)] = clock64();                                              \
   } while (0)
 #else
-#define PS_TC_TRACE3(k) \
-  do {                  \
-  } while (0)
-#define PS_TC_TRACE2(i, k) \
-  do {                     \
-  } while (0)
 #define PS_TC_TRACE(slot, cond) \
   do {                          \
   } while (0)
@@ -368,10 +351,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int jj = i - grp * WJ;
         const int sw = grp % WG;
         const int sa = i % AS;
-        PS_TC_TRACE2(i, 0);
         if (!warp_wait(w_full(sw), (grp / WG) & 1, abort_flag, p.status)) break;
         PS_TC_TRACE(16 + (i & 255) * 8 + 5, t == 0);
-        PS_TC_TRACE2(i, 1);
         // widen in registers first: only the TMEM store waits for the stage
         uint32_t words[NSUB][kChunks * 8];
 #pragma unroll
@@ -388,27 +369,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             w8[4] = hi.x; w8[5] = hi.y; w8[6] = hi.z; w8[7] = hi.w;
           }
         }
-        PS_TC_TRACE2(i, 2);
         if (i >= AS && !warp_wait(a_empty(sa), ((i / AS) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         PS_TC_TRACE(16 + (i & 255) * 8 + 2, t == 0);
-        PS_TC_TRACE2(i, 3);
 #pragma unroll
         for (int sub = 0; sub < NSUB; ++sub) {
           const uint32_t ta = tlane + sa * C::kACols + sub * (kBK / 2);
           tmem_st16(ta, words[sub]);
           tmem_st16(ta + 16, words[sub] + 16);
         }
-        PS_TC_TRACE2(i, 4);
         tmem_wait_st();
-        PS_TC_TRACE2(i, 5);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(a_full(sa));
           mbar_arrive(w_empty(sw));
         }
-        PS_TC_TRACE2(i, 6);
         PS_TC_TRACE(16 + (i & 255) * 8 + 3, t == 0);
       }
     }
@@ -459,9 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
           for (int c = 32 * h; c < BM; c += 64) {
             float v[32];
-            PS_TC_TRACE3(sub * 32 + (c / 64) * 4 + 0);
             if (ok) tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + sub * BM + c, v);
-            PS_TC_TRACE3(sub * 32 + (c / 64) * 4 + 1);
             if (use_tma && p.swiglu) {
               // lanes 2k / 2k+1 hold gate / up of intermediate channel
               // (n0 + sub*128 + q*32)/2 + k: each rounded to dtype (the
@@ -508,11 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          PS_TC_TRACE3(sub * 32 + 20);
           if (use_tma) {
             fence_proxy_async();
             epi_bar();
-            PS_TC_TRACE3(sub * 32 + 21);
             if (threadIdx.x == 96) {
               if (p.swiglu) {
                 tma_store_2d(&om.y, out_sa + sub * BM * 128, (n0 + sub * 128) / 2, m0);
@@ -531,10 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        PS_TC_TRACE3(100);
         if (use_tma && threadIdx.x == 96) {
           bulk_wait_all();  // stores done (pushed outputs complete before the arrival below)
-          PS_TC_TRACE3(101);
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
       }
@@ -654,7 +624,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                   }
                 }
               }
-              PS_TC_TRACE3(102 + min(7, (m - r0) / (R * kRowStep)) * 2);
 #pragma unroll
               for (int u = 0; u < R; ++u) {
                 if (!live[u]) continue;
@@ -686,7 +655,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint4*>((p.push.world > 0 ? static_cast<T*>(p.push.dst[d]) : y) + off) = pk;
                 }
               }
-              PS_TC_TRACE3(103 + min(7, (m - r0) / (R * kRowStep)) * 2);
             }
           };
           if (p.ws && vec) {
@@ -1015,9 +983,6 @@ int launch_t(const CUtensorMap& wm, const CUtensorMap& xm, const TcParams& p, co
 #ifdef PS_TRACE
 extern "C" PS_API int ps_debug_tc_trace(unsigned long long* host, int n) {
   return static_cast<int>(cudaMemcpyFromSymbol(host, g_tc_trace, sizeof(unsigned long long) * n));
-}
-extern "C" PS_API int ps_debug_tc_trace2(unsigned long long* host, int n) {
-  return static_cast<int>(cudaMemcpyFromSymbol(host, g_tc_trace2, sizeof(unsigned long long) * n));
 }
 #endif
 
