@@ -52,6 +52,7 @@ def _weights(world, N, K, int8, dev, g):
     (1, 33, 256, 512, True),       # degenerate world of one
     (8, 17, 2048, 256, True),      # TP8 o_proj width
     (2, 9, 1024, 512, True),       # decode-sized: the mma.sync small-M linear pushes
+    (2, 4, 1024, 8192, True),      # decode-sized, long K: the cp.async-ring small-M linear pushes
 ])
 def test_push_then_allreduce_rmsnorm(world, M, N, K, int8):
     _need_gpu()

@@ -202,8 +202,11 @@ def test_quantize_per_channel_bit_exact(dev):
     assert rel_err(y.cpu().numpy(), g["y"]) < 1e-5
 
 
+# (96, 11008): few row groups and a long K, the small-M kernel's cp.async ring
+# at M <= 8; (9480, 880) and (4808, 1040): ragged in N (not a multiple of 16)
+# and K (not a multiple of 64), with 593 / 301 row groups
 @pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 64, 130])
-@pytest.mark.parametrize("NK", [(2560, 2048), (2048, 2048), (96, 11008), (136, 896)])
+@pytest.mark.parametrize("NK", [(2560, 2048), (2048, 2048), (96, 11008), (136, 896), (9480, 880), (4808, 1040)])
 def test_w8a16_linear_matches_oracle(dev, M, NK):
     from pageserve_b200.quantization import w8a16_linear
     N, K = NK
@@ -355,8 +358,8 @@ def test_tile_int8_weight_layout(dev, NK):
     assert np.array_equal(t, _tile_ref(q))
 
 
-@pytest.mark.parametrize("M", [1, 5, 64, 130, 576])
-@pytest.mark.parametrize("NK", [(2560, 2048), (136, 896), (300, 880), (2048, 11008)])
+@pytest.mark.parametrize("M", [1, 5, 16, 64, 130, 576])
+@pytest.mark.parametrize("NK", [(2560, 2048), (136, 896), (300, 880), (2048, 11008), (9480, 880), (4808, 1040)])
 def test_w8a16_linear_tiled_matches_oracle(dev, M, NK):
     from pageserve_b200.quantization import tile_int8_weight, w8a16_linear
     N, K = NK
@@ -412,7 +415,7 @@ def test_split_k_exchange_paths_agree(dev, MNK):
 
 
 @pytest.mark.parametrize("M", [1, 7, 64, 576])
-@pytest.mark.parametrize("IK", [(11008, 2048), (160, 256), (1376, 2048), (896, 640)])
+@pytest.mark.parametrize("IK", [(11008, 2048), (160, 256), (1376, 2048), (896, 640), (4744, 880), (160, 8192)])
 def test_linear_swiglu_matches_oracle(dev, M, IK):
     """engine/model.py:188-190: silu(gate) * up from one linear over the
     row-interleaved gate|up int8 weight; also equal to the unfused gate|up
