@@ -542,11 +542,16 @@ def run_gpu(args):
     for _ in range(args.warmup):
         g.replay()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     launches0 = _lib.launch_count()
+    # The clock sampler starts (and waits for its first sample, 0.1-1 s, a
+    # different time on every rank) before the barrier: with it between the
+    # barrier and the start event, the first collective of the early ranks
+    # waited for the late ones inside their timed window (N > 1 read slower
+    # than end to end).
     with Clocks(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         torch.cuda.nvtx.range_push("timed")
